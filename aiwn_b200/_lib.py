@@ -1,0 +1,186 @@
+"""ctypes binding of the C ABI in ``include/aiwn_il.h`` (``libaiwn_il.so``).
+
+The shared library is built in-tree by ``python -m aiwn_b200.csrc.build``
+(or ``__graft_entry__.build()``).  There is no fallback: if the library is
+missing or the tensors are not on a B200, every call raises ``ILError``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libaiwn_il.so")
+_lib = None
+_lock = threading.Lock()
+
+IL_F32, IL_BF16 = 0, 1
+_DTYPES = {torch.float32: IL_F32, torch.bfloat16: IL_BF16}
+
+
+class ILError(RuntimeError):
+    """A status other than IL_OK returned by the C ABI."""
+
+
+def library_path() -> str:
+    return _PATH
+
+
+def load():
+    """Load ``libaiwn_il.so`` once and declare its signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(_PATH):
+            raise ILError(f"{_PATH} is not built; run `python aiwn_b200/csrc/build.py`")
+        lib = ctypes.CDLL(_PATH)
+        vp, i64, f64, ci = ctypes.c_void_p, ctypes.c_int64, ctypes.c_double, ctypes.c_int
+        lib.il_status_string.argtypes = [ci]
+        lib.il_status_string.restype = ctypes.c_char_p
+        lib.il_version.argtypes = []
+        lib.il_version.restype = ctypes.c_char_p
+        lib.il_forward.argtypes = [vp, ci, vp, vp, vp, i64, i64, i64, i64, f64, vp]
+        lib.il_forward.restype = ci
+        lib.il_workspace_bytes.argtypes = [i64, i64, i64, i64, ci]
+        lib.il_workspace_bytes.restype = i64
+        lib.il_backward.argtypes = [vp, vp, ci, vp, vp, vp, vp, i64, i64, i64, i64, f64, vp, i64, vp]
+        lib.il_backward.restype = ci
+        lib.il_bins.argtypes = [vp, ci, i64, i64, i64, f64, vp, vp, vp, vp]
+        lib.il_bins.restype = ci
+        lib.il_adam_step.argtypes = [vp, vp, vp, vp, i64, f64, f64, f64, f64, i64, vp]
+        lib.il_adam_step.restype = ci
+        lib.il_kernel_launches.argtypes = []
+        lib.il_kernel_launches.restype = i64
+        lib.il_check_device_status.argtypes = [vp]
+        lib.il_check_device_status.restype = ci
+        _lib = lib
+    return _lib
+
+
+def available() -> bool:
+    """True when libaiwn_il.so loads and exports the full ABI."""
+    try:
+        load()
+        return True
+    except (ILError, OSError, AttributeError):
+        return False
+
+
+def version() -> str:
+    return load().il_version().decode()
+
+
+def _check(rc: int, what: str):
+    if rc != 0:
+        raise ILError(f"{what}: {load().il_status_string(rc).decode()} (status {rc})")
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(dev: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ILError("aiwn_b200 kernels need CUDA tensors; there is no CPU path")
+        if t is not None and not t.is_contiguous():
+            raise ILError("aiwn_b200 kernels need contiguous tensors")
+
+
+class _on_device:
+    """Make x's device current for the duration of a C call (cheap no-op when
+    it already is)."""
+
+    def __init__(self, dev: torch.device):
+        self.idx = dev.index if dev.index is not None else torch.cuda.current_device()
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.idx:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
+
+    def __exit__(self, *a):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+
+
+def x_dtype_code(x: torch.Tensor) -> int:
+    try:
+        return _DTYPES[x.dtype]
+    except KeyError:
+        raise ILError(f"x dtype {x.dtype} is not supported (float32 or bfloat16)") from None
+
+
+def forward(x, table, bias, out, bw: float):
+    """out[N, OUT] (fp32) <- IndexedLinear forward of x[N, IN]."""
+    _need_cuda(x, table, bias, out)
+    N, IN = x.shape
+    K, _, OUT = table.shape
+    lib = load()
+    with _on_device(x.device):
+        _check(lib.il_forward(_p(x), x_dtype_code(x), _p(table), _p(bias), _p(out),
+                              N, IN, OUT, K, float(bw), _stream(x.device)), "il_forward")
+    return out
+
+
+def workspace_bytes(N, IN, OUT, K, x_dtype: int) -> int:
+    return int(load().il_workspace_bytes(N, IN, OUT, K, x_dtype))
+
+
+def backward(go, x, table, gx, gt, gb, bw: float, workspace=None):
+    """gx / gt / gb (any may be None) <- gradients of the forward."""
+    _need_cuda(go, x, table, gx, gt, gb, workspace)
+    N, IN = x.shape
+    K, _, OUT = table.shape
+    lib = load()
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    with _on_device(x.device):
+        _check(lib.il_backward(_p(go), _p(x), x_dtype_code(x), _p(table), _p(gx), _p(gt), _p(gb),
+                               N, IN, OUT, K, float(bw), _p(workspace), ws_bytes,
+                               _stream(x.device)), "il_backward")
+
+
+def bins(x, K: int, bw: float):
+    """(lo int32, hi int32, fr fp32) of every element of x[N, IN]."""
+    _need_cuda(x)
+    x2 = x.reshape(x.shape[0] if x.dim() > 1 else 1, -1)
+    lo = torch.empty(x2.shape, dtype=torch.int32, device=x.device)
+    hi = torch.empty_like(lo)
+    fr = torch.empty(x2.shape, dtype=torch.float32, device=x.device)
+    with _on_device(x.device):
+        _check(load().il_bins(_p(x2), x_dtype_code(x), x2.shape[0], x2.shape[1], K, float(bw),
+                              _p(lo), _p(hi), _p(fr), _stream(x.device)), "il_bins")
+    return lo.reshape(x.shape), hi.reshape(x.shape), fr.reshape(x.shape)
+
+
+def adam_step(p, g, m, v, lr, beta1, beta2, eps, step: int):
+    _need_cuda(p, g, m, v)
+    for t in (p, g, m, v):
+        if t.dtype != torch.float32:
+            raise ILError("il_adam_step works on fp32 tensors")
+    with _on_device(p.device):
+        _check(load().il_adam_step(_p(p), _p(g), _p(m), _p(v), p.numel(), float(lr), float(beta1),
+                                   float(beta2), float(eps), int(step), _stream(p.device)),
+               "il_adam_step")
+
+
+def kernel_launches() -> int:
+    """Kernels launched by libaiwn_il.so in this process so far."""
+    return int(load().il_kernel_launches())
+
+
+def check_device_status(dev=None):
+    dev = torch.device("cuda", torch.cuda.current_device()) if dev is None else dev
+    with _on_device(dev):
+        _check(load().il_check_device_status(_stream(dev)), "device status")

@@ -1,0 +1,222 @@
+// il_capi.cu -- the extern "C" entry points declared in include/aiwn_il.h.
+//
+// Argument checking, kernel selection and launch.  All kernels are compiled
+// into this one translation unit (they are included below), so the library
+// needs no relocatable device code.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "../../include/aiwn_il.h"
+#include "il_common.cuh"
+#include "il_simple.cuh"
+#include "il_fast.cuh"
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+int g_dev_ok[kMaxDevices];  // 0 = unchecked, 1 = sm_100, -1 = other
+int g_num_sms[kMaxDevices];
+std::mutex g_dev_mu;
+
+int check_device(int* num_sms) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        return IL_ERR_DEVICE;
+    }
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (g_dev_ok[dev] == 0) {
+        int major = 0, minor = 0, sms = 0;
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (cudaGetLastError() != cudaSuccess) return IL_ERR_DEVICE;
+        // the fatbin holds sm_100a code only
+        g_dev_ok[dev] = (major == 10 && minor == 0) ? 1 : -1;
+        g_num_sms[dev] = sms > 0 ? sms : 1;
+    }
+    if (num_sms) *num_sms = g_num_sms[dev];
+    return g_dev_ok[dev] == 1 ? IL_OK : IL_ERR_DEVICE;
+}
+
+il::BinCfg make_cfg(double bw, int64_t K) {
+    il::BinCfg c;
+    c.bw = (float)bw;
+    c.K = (int)K;
+    int e = 0;
+    const float m = frexpf(c.bw, &e);
+    c.pow2 = (m == 0.5f) ? 1 : 0;  // bw == 2^(e-1) exactly
+    c.inv = c.pow2 ? ldexpf(1.0f, 1 - e) : 1.0f / c.bw;
+    return c;
+}
+
+int check_common(const void* x, int x_dtype, int64_t N, int64_t IN, int64_t K, double bw) {
+    if (x_dtype != IL_F32 && x_dtype != IL_BF16) return IL_ERR_DTYPE;
+    if (N < 0 || IN < 1 || K < 2 || K > (1 << 24)) return IL_ERR_SHAPE;
+    const float bwf = (float)bw;
+    if (!(bwf > 0.0f) || isinf(bwf)) return IL_ERR_VALUE;
+    if (N > 0 && !x) return IL_ERR_NULL;
+    return IL_OK;
+}
+
+std::atomic<int64_t> g_launches{0};
+
+// every kernel launch of the library is followed by this check
+inline int launch_status() {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? IL_OK : IL_ERR_LAUNCH;
+}
+
+inline unsigned grid_for(int64_t work, int threads, int num_sms) {
+    int64_t blocks = (work + threads - 1) / threads;
+    const int64_t cap = (int64_t)num_sms * 32;
+    if (blocks > cap) blocks = cap;
+    return (unsigned)(blocks < 1 ? 1 : blocks);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* il_status_string(int s) {
+    switch (s) {
+        case IL_OK: return "ok";
+        case IL_ERR_SHAPE: return "invalid shape";
+        case IL_ERR_DTYPE: return "invalid dtype";
+        case IL_ERR_ALIGN: return "misaligned pointer";
+        case IL_ERR_LAUNCH: return "CUDA launch or API error";
+        case IL_ERR_WORKSPACE: return "workspace missing or too small";
+        case IL_ERR_NULL: return "required pointer is NULL";
+        case IL_ERR_DEVICE: return "no sm_100 (B200) device current";
+        case IL_ERR_TIMEOUT: return "a device-side bounded wait gave up";
+        case IL_ERR_VALUE: return "invalid scalar argument";
+        default: return "unknown status";
+    }
+}
+
+const char* il_version(void) { return "aiwn_il 0.1.0 sm_100a"; }
+
+int il_forward(const void* x, int x_dtype, const float* table, const float* bias, float* out,
+               int64_t N, int64_t IN, int64_t OUT, int64_t K, double bw, void* stream) {
+    int st = check_common(x, x_dtype, N, IN, K, bw);
+    if (st) return st;
+    if (OUT < 1) return IL_ERR_SHAPE;
+    if (N == 0) return IL_OK;
+    if (!table || !bias || !out) return IL_ERR_NULL;
+    int sms = 0;
+    if ((st = check_device(&sms))) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    const il::BinCfg c = make_cfg(bw, K);
+    if (il::fast_forward_ok(x, x_dtype, table, bias, out, N, IN, OUT, K)) {
+        return il::fast_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s);
+    }
+    const unsigned g = grid_for(N * OUT, 256, sms);
+    if (x_dtype == IL_BF16)
+        il::fwd_simple_kernel<il::kBF16><<<g, 256, 0, s>>>(x, table, bias, out, N, IN, OUT, c);
+    else
+        il::fwd_simple_kernel<il::kF32><<<g, 256, 0, s>>>(x, table, bias, out, N, IN, OUT, c);
+    return launch_status();
+}
+
+int64_t il_workspace_bytes(int64_t N, int64_t IN, int64_t OUT, int64_t K, int x_dtype) {
+    return il::fast_backward_workspace(N, IN, OUT, K, x_dtype);
+}
+
+int il_backward(const float* go, const void* x, int x_dtype, const float* table, void* gx,
+                float* gt, float* gb, int64_t N, int64_t IN, int64_t OUT, int64_t K, double bw,
+                void* workspace, int64_t workspace_bytes, void* stream) {
+    int st = check_common(x, x_dtype, N, IN, K, bw);
+    if (st) return st;
+    if (OUT < 1) return IL_ERR_SHAPE;
+    if (!table) return IL_ERR_NULL;
+    if (N > 0 && !go) return IL_ERR_NULL;
+    int sms = 0;
+    if ((st = check_device(&sms))) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    const il::BinCfg c = make_cfg(bw, K);
+    const int64_t need = il::fast_backward_workspace(N, IN, OUT, K, x_dtype);
+    if (need > 0 && (!workspace || workspace_bytes < need)) return IL_ERR_WORKSPACE;
+    if (gt && cudaMemsetAsync(gt, 0, (size_t)(K * IN * OUT) * sizeof(float), s) != cudaSuccess)
+        return IL_ERR_LAUNCH;
+    if (gb && cudaMemsetAsync(gb, 0, (size_t)OUT * sizeof(float), s) != cudaSuccess)
+        return IL_ERR_LAUNCH;
+    if (N == 0) return IL_OK;
+    if (il::fast_backward_ok(go, x, x_dtype, table, gx, gt, gb, N, IN, OUT, K)) {
+        return il::fast_backward(go, x, x_dtype, table, gx, gt, gb, N, IN, OUT, c, workspace,
+                                 sms, s);
+    }
+    if (gx) {
+        const unsigned g = grid_for(N * IN, 256, sms);
+        if (x_dtype == IL_BF16)
+            il::dx_simple_kernel<il::kBF16><<<g, 256, 0, s>>>(go, x, table, gx, N, IN, OUT, c);
+        else
+            il::dx_simple_kernel<il::kF32><<<g, 256, 0, s>>>(go, x, table, gx, N, IN, OUT, c);
+        if ((st = launch_status())) return st;
+    }
+    if (gt) {
+        const unsigned g = grid_for(N * IN * OUT, 256, sms);
+        if (x_dtype == IL_BF16)
+            il::dtable_simple_kernel<il::kBF16><<<g, 256, 0, s>>>(go, x, gt, N, IN, OUT, c);
+        else
+            il::dtable_simple_kernel<il::kF32><<<g, 256, 0, s>>>(go, x, gt, N, IN, OUT, c);
+        if ((st = launch_status())) return st;
+    }
+    if (gb) {
+        const int64_t rows = 1024;
+        dim3 g((unsigned)((OUT + 31) / 32), (unsigned)((N + rows - 1) / rows));
+        il::dbias_simple_kernel<<<g, 256, 0, s>>>(go, gb, N, OUT, rows);
+        if ((st = launch_status())) return st;
+    }
+    return IL_OK;
+}
+
+int il_bins(const void* x, int x_dtype, int64_t N, int64_t IN, int64_t K, double bw, int32_t* lo,
+            int32_t* hi, float* fr, void* stream) {
+    int st = check_common(x, x_dtype, N, IN, K, bw);
+    if (st) return st;
+    if (N == 0) return IL_OK;
+    int sms = 0;
+    if ((st = check_device(&sms))) return st;
+    const il::BinCfg c = make_cfg(bw, K);
+    const unsigned g = grid_for(N * IN, 256, sms);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (x_dtype == IL_BF16)
+        il::bins_kernel<il::kBF16><<<g, 256, 0, s>>>(x, N * IN, c, lo, hi, fr);
+    else
+        il::bins_kernel<il::kF32><<<g, 256, 0, s>>>(x, N * IN, c, lo, hi, fr);
+    return launch_status();
+}
+
+int il_adam_step(float* p, const float* g, float* m, float* v, int64_t n, double lr, double beta1,
+                 double beta2, double eps, int64_t step, void* stream) {
+    if (n < 0 || step < 1) return IL_ERR_SHAPE;
+    if (n == 0) return IL_OK;
+    if (!p || !g || !m || !v) return IL_ERR_NULL;
+    int sms = 0;
+    int st = check_device(&sms);
+    if (st) return st;
+    const double bc1 = 1.0 - pow(beta1, (double)step);
+    const double bc2 = 1.0 - pow(beta2, (double)step);
+    const unsigned grid = grid_for(n, 256, sms);
+    il::adam_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
+        p, g, m, v, n, (float)beta1, (float)beta2, (float)eps, (float)(lr / bc1), (float)sqrt(bc2));
+    return launch_status();
+}
+
+int64_t il_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int il_check_device_status(void* stream) {
+    if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return IL_ERR_LAUNCH;
+    unsigned int h = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&h, il::g_il_error, sizeof(h)) != cudaSuccess) return IL_ERR_LAUNCH;
+    if (h) cudaMemcpyToSymbol(il::g_il_error, &zero, sizeof(zero));
+    return h ? IL_ERR_TIMEOUT : IL_OK;
+}
+
+}  // extern "C"

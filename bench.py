@@ -1,0 +1,409 @@
+"""IndexedLinear benchmark on B200: fwd and fwd+bwd tokens/s, % of HBM roofline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c3]
+
+One step = one forward + backward of IndexedLinear over the configuration's
+token batch (B*seq tokens per GPU; weak scaling across GPUs: with N>1 every
+rank processes its own batch and the [table | bias] gradient bucket is
+all-reduced over NCCL each step, the data-parallel exchange of training).
+Rank 0 prints one JSON line.  Inputs rotate over enough sets that the bytes
+read per step are not L2-resident (>126 MB per rotation).
+
+--impl reference times the reference's own CPU path (its eager PyTorch ops,
+restated in oracle/eager_port.py) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "fwd & fwd+bwd tokens/s at K=128/512, seq=4096; % of HBM roofline"
+L2_BYTES = 126 * 2**20
+
+# The benchmark configurations (d, K, B, seq as the reference's high_k sweep
+# names them; in_d = out_d = indexed_dims(d, 4d, K)[0]).
+CONFIGS = {
+    "c3": dict(desc="high-K headline: IndexedLinear(20, 20, K=512) fwd+bwd, d=512 B=32 seq=4096, "
+                    "x~U(-1,1) fp32, table~N(0,1/in_d)", d=512, K=512, B=32, seq=4096, IN=20, OUT=20,
+               xdist="uniform", dtype="f32"),
+    "c2": dict(desc="sweep point: IndexedLinear(20, 20, K=128) fwd+bwd, d=256 B=32 seq=4096, "
+                    "x=tanh(N(0,1)) bf16, fp32 table", d=256, K=128, B=32, seq=4096, IN=20, OUT=20,
+               xdist="tanh_normal", dtype="bf16"),
+    "c1": dict(desc="IndexedLinear(64, 64, K=16) fwd+bwd, d=256 B=8 seq=256, x~U(-1,1) fp32",
+               d=256, K=16, B=8, seq=256, IN=64, OUT=64, xdist="uniform", dtype="f32"),
+    "c3ref": dict(desc="reference benchmark shape IndexedLinear(20, 80, K=512), B=32 seq=4096 fp32",
+                  d=512, K=512, B=32, seq=4096, IN=20, OUT=80, xdist="uniform", dtype="f32"),
+    "c4": dict(desc="IndexedLinear(1024, 1024, K=64), 16384 tokens per GPU, x=clamp(N(0,0.5)) fp32",
+               d=1024, K=64, B=2, seq=8192, IN=1024, OUT=1024, xdist="clamp_normal", dtype="f32"),
+}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def algorithmic_bytes(N, IN, OUT, K, sx):
+    """Compulsory HBM bytes: x, out, table, bias for the forward; go, x, table
+    re-read and dx, dtable, dbias written for the backward."""
+    fwd = N * IN * sx + N * OUT * 4 + K * IN * OUT * 4 + OUT * 4
+    bwd = N * OUT * 4 + N * IN * sx + K * IN * OUT * 4 + N * IN * sx + K * IN * OUT * 4 + OUT * 4
+    return fwd, bwd
+
+
+def make_x(N, IN, xdist, dtype, gen, device):
+    if xdist == "uniform":
+        x = torch.rand(N, IN, generator=gen, device=device) * 2 - 1
+    elif xdist == "tanh_normal":
+        x = torch.tanh(torch.randn(N, IN, generator=gen, device=device))
+    else:
+        x = (torch.randn(N, IN, generator=gen, device=device) * 0.5).clamp(-1, 1)
+    return x.to(torch.bfloat16) if dtype == "bf16" else x
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed loops run."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(", ") for r in out.strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for k, name in enumerate(names):
+                    if r[5 + k].strip().lower() == "active":
+                        reasons.add(name)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        sm.sort()
+        # samples under load: the top half of the SM clock distribution is the
+        # timed region (the sampler also sees the idle edges around it)
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's eager CPU path on the host cores
+# ---------------------------------------------------------------------------
+
+def run_reference(args, cfg, world, rank):
+    if rank != 0:
+        return None
+    from oracle.eager_port import eager_step
+    torch.set_num_threads(os.cpu_count() or 1)
+    N, IN, OUT, K = cfg["B"] * cfg["seq"], cfg["IN"], cfg["OUT"], cfg["K"]
+    bw = 2.0 / K
+    g = torch.Generator().manual_seed(0)
+    table = torch.randn(K, IN, OUT, generator=g) / math.sqrt(IN)
+    bias = torch.zeros(OUT)
+    # size the per-step token sample so the whole run stays within ~2 minutes
+    probe = 1024
+    x = make_x(probe, IN, cfg["xdist"], cfg["dtype"], g, "cpu")
+    go = torch.randn(probe, OUT, generator=g)
+    eager_step(x, table, bias, go, bw)
+    t = time.perf_counter()
+    eager_step(x, table, bias, go, bw)
+    per_tok = (time.perf_counter() - t) / probe
+    budget = 100.0 / max(1, args.steps + args.warmup)
+    n_s = int(min(N, max(256, budget / max(per_tok, 1e-12))))
+    n_s = max(256, (n_s // 256) * 256)
+    x = make_x(n_s, IN, cfg["xdist"], cfg["dtype"], g, "cpu")
+    go = torch.randn(n_s, OUT, generator=g)
+    for _ in range(args.warmup):
+        eager_step(x, table, bias, go, bw)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eager_step(x, table, bias, go, bw)
+    dt = (time.perf_counter() - t0) / args.steps
+    v = n_s / dt
+    cores = torch.get_num_threads()
+    sample = (f"{n_s} of the {N} tokens of the workload per step (fwd+bwd of the reference's "
+              f"eager ops, restated in oracle/eager_port.py), {cores} threads")
+    return {
+        "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16" if cfg["dtype"] == "bf16" else "f32", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": cfg["desc"], "K": K, "in_d": IN, "out_d": OUT, "tokens_per_gpu": N,
+                   "d": cfg["d"], "B": cfg["B"], "seq": cfg["seq"]},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def cpu_baseline(cfg, seconds=12.0):
+    """The reference's CPU path on a bounded sample of the workload."""
+    from oracle.eager_port import eager_step
+    torch.set_num_threads(os.cpu_count() or 1)
+    IN, OUT, K = cfg["IN"], cfg["OUT"], cfg["K"]
+    bw = 2.0 / K
+    g = torch.Generator().manual_seed(0)
+    table = torch.randn(K, IN, OUT, generator=g) / math.sqrt(IN)
+    bias = torch.zeros(OUT)
+    n_s = 4096 if IN * OUT <= 4096 else 32
+    x = make_x(n_s, IN, cfg["xdist"], cfg["dtype"], g, "cpu")
+    go = torch.randn(n_s, OUT, generator=g)
+    eager_step(x, table, bias, go, bw)
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        eager_step(x, table, bias, go, bw)
+        done += 1
+    dt = (time.perf_counter() - t0) / done
+    cores = torch.get_num_threads()
+    return {"value": n_s / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{done} fwd+bwd steps of {n_s} tokens (reference eager ops, "
+                      f"oracle/eager_port.py) in {seconds:.0f} s on {cores} threads"}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, cfg, world, rank, local):
+    from aiwn_b200 import IndexedLinear, _lib
+    from aiwn_b200.distributed import TokenParallelIndexedLinear
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    N, IN, OUT, K = cfg["B"] * cfg["seq"], cfg["IN"], cfg["OUT"], cfg["K"]
+    bw = 2.0 / K
+    sx = 2 if cfg["dtype"] == "bf16" else 4
+    xdt = _lib.x_dtype_code(torch.empty(0, dtype=torch.bfloat16 if sx == 2 else torch.float32))
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    per_set = N * IN * sx * 2 + N * OUT * 4 * 2  # x, dx, go, out
+    n_sets = max(2, min(16, math.ceil(2 * L2_BYTES / per_set)))
+    xs = [make_x(N, IN, cfg["xdist"], cfg["dtype"], gen, dev) for _ in range(n_sets)]
+    gos = [torch.randn(N, OUT, generator=gen, device=dev) for _ in range(n_sets)]
+    outs = [torch.empty(N, OUT, device=dev) for _ in range(n_sets)]
+    gxs = [torch.empty_like(x) for x in xs]
+    table = torch.randn(K, IN, OUT, generator=gen, device=dev) / math.sqrt(IN)
+    if world > 1:
+        import torch.distributed as dist
+        dist.broadcast(table, 0)
+    bias = torch.zeros(OUT, device=dev)
+    bucket = torch.empty(K * IN * OUT + OUT, device=dev)  # [gt | gb], all-reduced as one buffer
+    gt = bucket[: K * IN * OUT].view(K, IN, OUT)
+    gb = bucket[K * IN * OUT:]
+    ws_n = _lib.workspace_bytes(N, IN, OUT, K, xdt)
+    ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
+
+    def step(k):
+        i = k % n_sets
+        _lib.forward(xs[i], table, bias, outs[i], bw)
+        _lib.backward(gos[i], xs[i], table, gxs[i], gt, gb, bw, ws if ws_n else None)
+        if world > 1:
+            torch.distributed.all_reduce(bucket)
+
+    def sync_all():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    clocks = ClockSampler(local) if rank == 0 else None
+
+    for k in range(max(3, args.warmup)):
+        step(k)
+    sync_all()
+    if clocks:
+        clocks.start()
+    launches0 = _lib.kernel_launches()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sync_all()
+    ev0.record()
+    for k in range(args.steps):
+        step(k)
+    ev1.record()
+    sync_all()
+    launches = _lib.kernel_launches() - launches0
+    ms_step = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+
+    # per-call device time of the forward and of the backward (same stream)
+    def time_calls(fn, reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        sync_all()
+        e0.record()
+        for k in range(reps):
+            fn(k)
+        e1.record()
+        sync_all()
+        return max_over_ranks(e0.elapsed_time(e1) / reps)
+
+    reps = max(args.steps, 20)
+    ms_fwd = time_calls(lambda k: _lib.forward(xs[k % n_sets], table, bias, outs[k % n_sets], bw), reps)
+    ms_bwd = time_calls(lambda k: _lib.backward(gos[k % n_sets], xs[k % n_sets], table, gxs[k % n_sets],
+                                                gt, gb, bw, ws if ws_n else None), reps)
+
+    # training step with the fused Adam update of table and bias
+    m_t, v_t = torch.zeros_like(bucket), torch.zeros_like(bucket)
+    params = torch.cat([table.reshape(-1), bias])
+
+    def train_step(k):
+        step(k)
+        _lib.adam_step(params, bucket, m_t, v_t, 1e-3, 0.9, 0.999, 1e-8, k + 1)
+
+    ms_train = time_calls(train_step, reps)
+
+    # end to end through the public module API, host buffers, copies inside
+    m = TokenParallelIndexedLinear(IN, OUT, K, layer=IndexedLinear(IN, OUT, K)).to(dev)
+    with torch.no_grad():
+        m.table.copy_(table)
+    xh = [x.cpu().pin_memory() for x in xs[:2]]
+    goh = [g.cpu().pin_memory() for g in gos[:2]]
+    outh = [torch.empty(N, OUT).pin_memory() for _ in range(2)]
+    gxh = [torch.empty(N, IN, dtype=xs[0].dtype).pin_memory() for _ in range(2)]
+    xd = torch.empty_like(xs[0])
+    god = torch.empty_like(gos[0])
+
+    def e2e_step(k):
+        i = k % 2
+        xd.copy_(xh[i], non_blocking=True)
+        god.copy_(goh[i], non_blocking=True)
+        xr = xd.detach().requires_grad_(True)
+        m.zero_grad()
+        y = m(xr)
+        y.backward(god)
+        if world > 1:
+            m.sync_grads()
+        outh[i].copy_(y.detach(), non_blocking=True)
+        gxh[i].copy_(xr.grad, non_blocking=True)
+
+    for k in range(3):
+        e2e_step(k)
+    e2e_reps = max(10, min(args.steps, 200))
+    ms_e2e = time_calls(e2e_step, e2e_reps)
+    clk = clocks.stop() if clocks else None
+
+    if rank != 0:
+        return None
+    hbm, peak_kind = peaks()
+    b_fwd, b_bwd = algorithmic_bytes(N, IN, OUT, K, sx)
+    dom = ("forward", ms_fwd, b_fwd) if ms_fwd >= ms_bwd else ("backward", ms_bwd, b_bwd)
+    achieved = dom[2] / (dom[1] * 1e-3) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        traffic = json.load(open(tp)).get(f"{args.config}:{dom[0]}")
+    res = {
+        "metric": METRIC,
+        "value": world * N / (ms_step * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16" if sx == 2 else "f32", "data": "synthetic",
+        "config": {"workload": cfg["desc"], "K": K, "in_d": IN, "out_d": OUT, "tokens_per_gpu": N,
+                   "d": cfg["d"], "B": cfg["B"], "seq": cfg["seq"], "x_dtype": cfg["dtype"],
+                   "parallelism": f"token-parallel dp{world}" + (" + NCCL all-reduce of [dtable|dbias]" if world > 1 else ""),
+                   "l2": f"inputs rotate over {n_sets} sets of x/go/out/dx ({n_sets * per_set / 2**20:.0f} MiB > L2)"},
+        "fwd_tokens_per_s": world * N / (ms_fwd * 1e-3),
+        "fwd_bwd_tokens_per_s": world * N / (ms_step * 1e-3),
+        "train_step_tokens_per_s": world * N / (ms_train * 1e-3),
+        "ms": {"fwd": ms_fwd, "bwd": ms_bwd, "fwd_bwd": ms_step, "train_step_adam": ms_train},
+        "hbm_roofline_frac": {
+            "fwd": b_fwd / (ms_fwd * 1e-3) / 1e9 / hbm,
+            "fwd_bwd": (b_fwd + b_bwd) / (ms_step * 1e-3) / 1e9 / hbm,
+        },
+        "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": dom[2]},
+        "e2e": {"value": world * N / (ms_e2e * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": xh[0].numel() * xh[0].element_size() + goh[0].numel() * 4,
+                "d2h_bytes_per_step": N * OUT * 4 + gxh[0].numel() * gxh[0].element_size(),
+                "api": "aiwn_b200 IndexedLinear (TokenParallelIndexedLinear wrapper) forward+backward"
+                       "(+gradient all-reduce when N>1); pinned host x/go in, out/dx out"},
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(cfg)
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c3")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            res = run_reference(args, cfg, world, rank)
+        else:
+            res = run_ours(args, cfg, world, rank, local)
+        if rank == 0 and res is not None:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1 and args.impl == "ours":
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

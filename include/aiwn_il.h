@@ -1,0 +1,137 @@
+/*
+ * aiwn_il.h -- C ABI of the B200 (sm_100a) IndexedLinear kernels.
+ *
+ * Drop-in boundary for the reference's GPU path of IndexedLinear
+ * (capbrady92-svg/AIWN).  Every entry point takes plain device pointers,
+ * int64 sizes, an explicit dtype code and a cudaStream_t (passed as void*),
+ * and returns an il_status (0 = success).  No entry point allocates device
+ * memory: outputs and workspaces are provided by the caller.  All kernels
+ * are enqueued on `stream`; nothing synchronises the host.
+ *
+ * Shapes (row-major, contiguous):
+ *   x      [N, IN]        fp32 or bf16           (IL_F32 / IL_BF16)
+ *   table  [K, IN, OUT]   fp32
+ *   bias   [OUT]          fp32
+ *   out    [N, OUT]       fp32   (fp32 also for bf16 x, as the reference's
+ *                                 eager path promotes against the fp32 table)
+ *   go     [N, OUT]       fp32
+ *   gx     [N, IN]        same dtype as x
+ *   gt     [K, IN, OUT]   fp32
+ *   gb     [OUT]          fp32
+ * bw is the bucket width the reference passes as a Python float (2/K); it
+ * is used as the fp32 value (float)bw, exactly as the reference's tensors do.
+ *
+ * Reference interfaces replaced (paths inside the reference repository):
+ *   il_forward        aiwn/layers/indexed_linear.py:101-113 (_Fn.forward:
+ *                     Triton _fwd, IL:23-39, then `out + bias`) and
+ *                     aiwn/layers/indexed_linear_cuda.cu:192-221
+ *                     (pybind `forward(x, table, bias, bw)`, cu:274-276)
+ *   il_backward       aiwn/layers/indexed_linear.py:115-151 (_Fn.backward:
+ *                     Triton _bwd_x IL:41-60 for gx, one-hot einsum
+ *                     IL:131-149 for gt, go.sum(0) IL:151 for gb) and
+ *                     aiwn/layers/indexed_linear_cuda.cu:224-267
+ *                     (pybind `backward(go, x, table, bw)`, cu:277-279)
+ *   il_bins           the bucketing of aiwn/layers/indexed_linear.py:175-177
+ *                     (exposed on its own for the bit-exact bin tests)
+ *   il_adam_step      torch.optim.Adam as used for the table and bias in the
+ *                     reference's training loops (aiwn/training/regression.py:75,
+ *                     transformer_validation.py:391)
+ * Semantics follow the reference's eager path (IndexedLinear._eager,
+ * aiwn/layers/indexed_linear.py:173-182, and autograd's backward of it),
+ * which clamps the low bin at 0 and masks the gradient's slope term where
+ * the interpolation fraction was clamped; the reference's Triton and CUDA
+ * kernels do neither.
+ */
+#ifndef AIWN_IL_H
+#define AIWN_IL_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define IL_API __attribute__((visibility("default")))
+#else
+#define IL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    IL_OK = 0,
+    IL_ERR_SHAPE = 1,       /* a size is negative, zero where it must not be, or too large */
+    IL_ERR_DTYPE = 2,       /* unknown dtype code */
+    IL_ERR_ALIGN = 3,       /* a pointer is not aligned as the kernels require */
+    IL_ERR_LAUNCH = 4,      /* a CUDA launch or API call failed (cudaGetLastError) */
+    IL_ERR_WORKSPACE = 5,   /* workspace missing or smaller than il_workspace_bytes() */
+    IL_ERR_NULL = 6,        /* a required pointer is NULL */
+    IL_ERR_DEVICE = 7,      /* no usable sm_100 device, or the kernel image does not match */
+    IL_ERR_TIMEOUT = 8,     /* a kernel's bounded wait gave up (reported by il_check_device_status) */
+    IL_ERR_VALUE = 9        /* an invalid scalar argument (e.g. bw <= 0, K < 2) */
+} il_status;
+
+typedef enum { IL_F32 = 0, IL_BF16 = 1 } il_dtype;
+
+/* Human-readable text of a status code (static storage). */
+IL_API const char* il_status_string(int status);
+
+/* Library version, e.g. "aiwn_il 0.1.0 sm_100a". */
+IL_API const char* il_version(void);
+
+/*
+ * Forward: out = sum_i x[n,i] * lerp(T[lo,i,:], T[hi,i,:], fr) + bias.
+ * Replaces aiwn/layers/indexed_linear.py:101-113 and
+ * aiwn/layers/indexed_linear_cuda.cu:192-221.
+ */
+IL_API int il_forward(const void* x, int x_dtype, const float* table, const float* bias, float* out,
+               int64_t N, int64_t IN, int64_t OUT, int64_t K, double bw, void* stream);
+
+/*
+ * Bytes of device workspace il_backward needs for these sizes (0 if none).
+ */
+IL_API int64_t il_workspace_bytes(int64_t N, int64_t IN, int64_t OUT, int64_t K, int x_dtype);
+
+/*
+ * Backward.  Any of gx / gt / gb may be NULL to skip that gradient.
+ * gt and gb are overwritten (not accumulated into).
+ * Replaces aiwn/layers/indexed_linear.py:115-151 and
+ * aiwn/layers/indexed_linear_cuda.cu:224-267.
+ */
+IL_API int il_backward(const float* go, const void* x, int x_dtype, const float* table, void* gx,
+                float* gt, float* gb, int64_t N, int64_t IN, int64_t OUT, int64_t K, double bw,
+                void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * Bins of every x element: lo (int32), hi (int32), fr (fp32); any output may
+ * be NULL.  Bit-exact with aiwn/layers/indexed_linear.py:175-177.
+ */
+IL_API int il_bins(const void* x, int x_dtype, int64_t N, int64_t IN, int64_t K, double bw, int32_t* lo,
+            int32_t* hi, float* fr, void* stream);
+
+/*
+ * One fused Adam step over `n` fp32 parameters (torch.optim.Adam semantics,
+ * no weight decay, no amsgrad):  m = b1 m + (1-b1) g;  v = b2 v + (1-b2) g^2;
+ * p -= lr/(1-b1^step) * m / (sqrt(v)/sqrt(1-b2^step) + eps).
+ */
+IL_API int il_adam_step(float* p, const float* g, float* m, float* v, int64_t n, double lr, double beta1,
+                 double beta2, double eps, int64_t step, void* stream);
+
+/*
+ * Number of kernels this library has launched in the process so far
+ * (host-side counter, all devices and threads).  Lets a caller count the
+ * library's launches inside a timed region.
+ */
+IL_API int64_t il_kernel_launches(void);
+
+/*
+ * Reads (and clears) the device-side error word that kernels set when a
+ * bounded wait gives up; returns IL_OK or IL_ERR_TIMEOUT.  Synchronises
+ * `stream`.
+ */
+IL_API int il_check_device_status(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AIWN_IL_H */

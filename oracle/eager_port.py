@@ -1,0 +1,36 @@
+"""Torch restatement of the reference's CPU path -- TEST/BENCH INFRASTRUCTURE ONLY.
+
+``IndexedLinear._eager`` (aiwn/layers/indexed_linear.py:173-182) is the
+reference's ``--device cpu`` implementation.  Its steps are restated here
+with the same ATen operations (so the host cores do the same work the
+reference does on CPU), and ``eager_step`` adds autograd's backward, as the
+reference's own step benchmark does (aiwn/bench/timing.py:65-72).
+
+Only ``bench.py`` (its ``--impl reference`` arm and ``cpu_baseline`` leg)
+uses this module, to time the reference's CPU path beside the GPU kernels.
+The parity checker is the C oracle (``oracle/il_oracle.c``).
+"""
+from __future__ import annotations
+
+import torch
+
+
+def eager_forward(x: torch.Tensor, table: torch.Tensor, bias: torch.Tensor, bw: float) -> torch.Tensor:
+    K = table.shape[0]
+    N, IN = x.shape
+    lo = ((x + 1) / bw).long().clamp(0, K - 1)
+    hi = (lo + 1).clamp(max=K - 1)
+    fr = ((x - (-1 + lo.float() * bw)) / bw).clamp(0, 1)
+    cols = torch.arange(IN, device=x.device).unsqueeze(0).expand(N, -1)
+    w = table[lo, cols] * (1 - fr.unsqueeze(-1)) + table[hi, cols] * fr.unsqueeze(-1)
+    return (w * x.unsqueeze(-1)).sum(1) + bias
+
+
+def eager_step(x, table, bias, go, bw):
+    """fwd + bwd of the eager path: returns (out, gx, gt, gb)."""
+    xl = x.detach().requires_grad_(True)
+    tl = table.detach().requires_grad_(True)
+    bl = bias.detach().requires_grad_(True)
+    out = eager_forward(xl, tl, bl, bw)
+    out.backward(go)
+    return out.detach(), xl.grad, tl.grad, bl.grad

@@ -1,0 +1,74 @@
+"""The C-ABI library loads and exports every symbol include/aiwn_il.h declares;
+argument checks that happen before any device work (no GPU needed)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from aiwn_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    src = open(os.path.join(ROOT, "include", "aiwn_il.h")).read()
+    return sorted(set(re.findall(r"IL_API\s+[\w\s\*]+?\b(il_\w+)\s*\(", src)))
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    for n in ("il_forward", "il_backward", "il_bins", "il_workspace_bytes", "il_adam_step",
+              "il_status_string", "il_version", "il_check_device_status", "il_kernel_launches"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(_lib.library_path())
+    for n in declared_symbols():
+        assert hasattr(lib, n), n
+
+
+def test_version_and_status_strings():
+    assert "sm_100a" in _lib.version()
+    lib = _lib.load()
+    assert lib.il_status_string(0) == b"ok"
+    for code in range(1, 10):
+        assert lib.il_status_string(code) not in (b"ok", b"unknown status")
+    assert lib.il_status_string(999) == b"unknown status"
+
+
+@pytest.mark.parametrize("args,code", [
+    # x_dtype invalid
+    (dict(x_dtype=7), 2),
+    # K < 2, IN < 1, OUT < 1, N < 0
+    (dict(K=1), 1), (dict(IN=0), 1), (dict(OUT=0), 1), (dict(N=-1), 1),
+    # bw not positive / not finite
+    (dict(bw=0.0), 9), (dict(bw=-1.0), 9), (dict(bw=float("inf")), 9),
+    # NULL x with N > 0
+    (dict(x=None), 6),
+])
+def test_forward_argument_checks(args, code):
+    lib = _lib.load()
+    a = dict(x=ctypes.c_void_p(16), x_dtype=0, N=4, IN=3, OUT=2, K=8, bw=0.25)
+    a.update(args)
+    rc = lib.il_forward(a["x"], a["x_dtype"], ctypes.c_void_p(16), ctypes.c_void_p(16),
+                        ctypes.c_void_p(16), a["N"], a["IN"], a["OUT"], a["K"], a["bw"], None)
+    assert rc == code
+
+
+def test_forward_empty_batch_is_noop():
+    lib = _lib.load()
+    assert lib.il_forward(None, 0, None, None, None, 0, 3, 2, 8, 0.25, None) == 0
+
+
+def test_adam_argument_checks():
+    lib = _lib.load()
+    assert lib.il_adam_step(None, None, None, None, 0, 1e-3, 0.9, 0.999, 1e-8, 1, None) == 0
+    assert lib.il_adam_step(None, None, None, None, 4, 1e-3, 0.9, 0.999, 1e-8, 0, None) == 1
+    assert lib.il_adam_step(None, None, None, None, 4, 1e-3, 0.9, 0.999, 1e-8, 1, None) == 6
+
+
+def test_workspace_query_is_host_only():
+    n = _lib.workspace_bytes(131072, 20, 20, 512, 0)
+    assert n >= 0

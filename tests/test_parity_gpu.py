@@ -1,0 +1,179 @@
+"""Parity of the CUDA kernels (through the C ABI) with the oracle and with the
+golden vectors of the reference.
+
+Tolerances (normwise, see golden_io.normwise_close): forward 1e-5 relative in
+fp32 and 2e-2 with bf16 x; fp32 gradients 1e-4; bf16 gx 2e-2.  Bins are
+bit-exact.
+"""
+import numpy as np
+import pytest
+import torch
+
+from golden_io import bins_names, case_names, load_bins, load_case, normwise_close
+from il_cases import CASES, EDGE_CASES, make_inputs, to_numpy_grad, x_numpy
+from oracle import oracle
+
+import aiwn_b200
+from aiwn_b200 import IndexedLinear, _Fn, _lib
+
+pytestmark = pytest.mark.gpu
+
+FWD_RTOL = {"f32": 1e-5, "bf16": 2e-2}
+GRAD_RTOL = 1e-4
+BF16_GX_RTOL = 2e-2
+DEV = "cuda"
+
+
+def _bf16_from_bits(b):
+    return torch.from_numpy(np.ascontiguousarray(b).view(np.int16)).view(torch.bfloat16)
+
+
+def run_ours(x, table, bias, go, bw):
+    """forward + backward through _Fn (the reference's autograd.Function API)."""
+    xg = x.to(DEV).requires_grad_(True)
+    tg = table.to(DEV).requires_grad_(True)
+    bg = bias.to(DEV).requires_grad_(True)
+    out = _Fn.apply(xg, tg, bg, bw)
+    out.backward(go.to(DEV))
+    torch.cuda.synchronize()
+    return out.detach(), xg.grad, tg.grad, bg.grad
+
+
+def check_against_oracle(c, x, table, bias, go):
+    bw = 2.0 / c.K
+    out, gx, gt, gb = run_ours(x, table, bias, go, bw)
+    assert out.dtype == torch.float32 and gx.dtype == x.dtype
+    xn = x_numpy(x)
+    ref = oracle.forward(xn, table.numpy(), bias.numpy(), bw, x_dtype=c.dtype)
+    normwise_close(out.cpu().numpy(), ref, FWD_RTOL[c.dtype], f"{c.name} out")
+    rgx, rgt, rgb = oracle.backward(go.numpy(), xn, table.numpy(), bw, x_dtype=c.dtype)
+    normwise_close(to_numpy_grad(gx), rgx, BF16_GX_RTOL if c.dtype == "bf16" else GRAD_RTOL, f"{c.name} gx")
+    normwise_close(gt.cpu().numpy(), rgt, GRAD_RTOL, f"{c.name} gt")
+    normwise_close(gb.cpu().numpy(), rgb, GRAD_RTOL, f"{c.name} gb")
+    lo, hi, fr = _lib.bins(x.to(DEV), c.K, bw)
+    rlo, rhi, rfr = oracle.bins(xn, c.K, bw, x_dtype=c.dtype)
+    assert np.array_equal(lo.cpu().numpy(), rlo) and np.array_equal(hi.cpu().numpy(), rhi)
+    assert np.array_equal(fr.cpu().numpy().view(np.uint32), rfr.view(np.uint32))
+
+
+@pytest.mark.parametrize("c", CASES + EDGE_CASES, ids=lambda c: c.name)
+def test_parity_vs_oracle(c):
+    x, table, bias, go = make_inputs(c)
+    check_against_oracle(c, x, table, bias, go)
+
+
+@pytest.mark.parametrize("name", case_names())
+def test_parity_vs_golden(name):
+    d = load_case(name)
+    dt = d["x_dtype"]
+    x = _bf16_from_bits(d["x"]) if dt == "bf16" else torch.from_numpy(d["x"])
+    out, gx, gt, gb = run_ours(x, torch.from_numpy(d["table"]), torch.from_numpy(d["bias"]),
+                               torch.from_numpy(d["go"]), d["bw"])
+    normwise_close(out.cpu().numpy(), d["out"], FWD_RTOL["f32"], "out")
+    normwise_close(to_numpy_grad(gx), d["gx"], BF16_GX_RTOL if dt == "bf16" else GRAD_RTOL, "gx")
+    normwise_close(gt.cpu().numpy(), d["gt"], GRAD_RTOL, "gt")
+    normwise_close(gb.cpu().numpy(), d["gb"], GRAD_RTOL, "gb")
+
+
+@pytest.mark.parametrize("name", bins_names())
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_bins_bit_exact_vs_golden(name, dt):
+    d = load_bins(name)
+    xb = d[f"x_{dt}"]
+    x = _bf16_from_bits(xb) if dt == "bf16" else torch.from_numpy(xb)
+    lo, hi, fr = _lib.bins(x.to(DEV), d["K"], d["bw"])
+    assert np.array_equal(lo.cpu().numpy(), d[f"lo_{dt}"])
+    assert np.array_equal(fr.cpu().numpy().view(np.uint32), d[f"fr_{dt}"].view(np.uint32))
+
+
+def test_forward_deterministic_and_token_independent():
+    """Full C3 size: bitwise-identical reruns, and the output of a token does
+    not depend on which other tokens share the launch."""
+    c = CASES[2]
+    x, table, bias, _ = make_inputs(c)
+    x, table, bias = x.to(DEV), table.to(DEV), bias.to(DEV)
+    bw = 2.0 / c.K
+    o1 = torch.empty(c.N, c.OUT, device=DEV)
+    o2 = torch.empty_like(o1)
+    _lib.forward(x, table, bias, o1, bw)
+    _lib.forward(x, table, bias, o2, bw)
+    assert torch.equal(o1, o2)
+    cut = 50001
+    oa = torch.empty(cut, c.OUT, device=DEV)
+    ob = torch.empty(c.N - cut, c.OUT, device=DEV)
+    _lib.forward(x[:cut].contiguous(), table, bias, oa, bw)
+    _lib.forward(x[cut:].contiguous(), table, bias, ob, bw)
+    assert torch.equal(torch.cat([oa, ob]), o1)
+
+
+def test_dtable_is_additive_over_token_chunks():
+    c = CASES[2]
+    x, table, bias, go = make_inputs(c)
+    x, table, go = x.to(DEV), table.to(DEV), go.to(DEV)
+    bw = 2.0 / c.K
+    gt = torch.empty_like(table)
+    _lib.backward(go, x, table, None, gt, None, bw, _ws(c, x))
+    parts = torch.zeros_like(table)
+    for a, b in ((0, 40000), (40000, 90001), (90001, c.N)):
+        g = torch.empty_like(table)
+        xs = x[a:b].contiguous()
+        _lib.backward(go[a:b].contiguous(), xs, table, None, g, None, bw, _ws(c, xs))
+        parts += g
+    normwise_close(parts.cpu().numpy(), gt.cpu().numpy(), GRAD_RTOL, "dtable chunks")
+
+
+def _ws(c, x):
+    n = _lib.workspace_bytes(x.shape[0], c.IN, c.OUT, c.K, _lib.x_dtype_code(x))
+    return torch.empty(n, dtype=torch.uint8, device=DEV) if n else None
+
+
+def test_module_flattens_leading_dims_and_backprops():
+    torch.manual_seed(0)
+    m = IndexedLinear(20, 80, 512).to(DEV)
+    with torch.no_grad():
+        m.bias.normal_()
+    x = (torch.rand(2, 3, 50, 20, device=DEV) * 2 - 1).requires_grad_(True)
+    y = m(x)
+    assert y.shape == (2, 3, 50, 80) and y.dtype == torch.float32
+    go = torch.randn_like(y)
+    y.backward(go)
+    xf = x.detach().reshape(-1, 20).cpu().numpy()
+    ref = oracle.forward(xf, m.table.detach().cpu().numpy(), m.bias.detach().cpu().numpy(), m.bw)
+    normwise_close(y.detach().reshape(-1, 80).cpu().numpy(), ref, 1e-5, "module out")
+    rgx, rgt, rgb = oracle.backward(go.reshape(-1, 80).cpu().numpy(), xf, m.table.detach().cpu().numpy(), m.bw)
+    normwise_close(x.grad.reshape(-1, 20).cpu().numpy(), rgx, GRAD_RTOL, "module gx")
+    normwise_close(m.table.grad.cpu().numpy(), rgt, GRAD_RTOL, "module gt")
+    normwise_close(m.bias.grad.cpu().numpy(), rgb, GRAD_RTOL, "module gb")
+    assert aiwn_b200.TRITON_OK and aiwn_b200.triton_available()
+
+
+def test_grad_subsets_follow_needs_input_grad():
+    c = CASES[0]
+    x, table, bias, go = make_inputs(c)
+    xg = x.to(DEV)
+    tg = table.to(DEV).requires_grad_(True)
+    out = _Fn.apply(xg, tg, bias.to(DEV), 2.0 / c.K)
+    out.backward(go.to(DEV))
+    _, rgt, _ = oracle.backward(go.numpy(), x.numpy(), table.numpy(), 2.0 / c.K)
+    normwise_close(tg.grad.cpu().numpy(), rgt, GRAD_RTOL, "gt only")
+
+
+def test_adam_step_matches_torch():
+    g = torch.Generator().manual_seed(5)
+    p0 = torch.randn(513 * 20 * 20 + 3, generator=g)
+    grads = [torch.randn(p0.shape, generator=g) for _ in range(3)]
+    ref = p0.clone().requires_grad_(True)
+    opt = torch.optim.Adam([ref], lr=1e-2, foreach=False)
+    p = p0.to(DEV)
+    m = torch.zeros_like(p)
+    v = torch.zeros_like(p)
+    for k, gr in enumerate(grads, start=1):
+        ref.grad = gr.clone()
+        opt.step()
+        _lib.adam_step(p, gr.to(DEV), m, v, 1e-2, 0.9, 0.999, 1e-8, k)
+    torch.cuda.synchronize()
+    normwise_close(p.cpu().numpy(), ref.detach().numpy(), 1e-6, "adam")
+
+
+def test_device_status_clean():
+    _lib.check_device_status()
