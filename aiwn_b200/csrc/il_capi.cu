@@ -113,8 +113,15 @@ int il_forward(const void* x, int x_dtype, const float* table, const float* bias
     if ((st = check_device(&sms))) return st;
     cudaStream_t s = (cudaStream_t)stream;
     const il::BinCfg c = make_cfg(bw, K);
-    if (il::fast_forward_ok(x, x_dtype, table, bias, out, N, IN, OUT, K)) {
-        return il::fast_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s);
+    if (il::fast_forward_ok(x, x_dtype, table, bias, out, N, IN, OUT, K, c)) {
+        const int rc = il::fast_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s);
+        if (rc != il::kNotApplicable) {
+            if (rc) {
+                cudaGetLastError();
+                return IL_ERR_LAUNCH;
+            }
+            return launch_status();
+        }
     }
     const unsigned g = grid_for(N * OUT, 256, sms);
     if (x_dtype == IL_BF16)
@@ -148,8 +155,15 @@ int il_backward(const float* go, const void* x, int x_dtype, const float* table,
         return IL_ERR_LAUNCH;
     if (N == 0) return IL_OK;
     if (il::fast_backward_ok(go, x, x_dtype, table, gx, gt, gb, N, IN, OUT, K)) {
-        return il::fast_backward(go, x, x_dtype, table, gx, gt, gb, N, IN, OUT, c, workspace,
-                                 sms, s);
+        const int rc =
+            il::fast_backward(go, x, x_dtype, table, gx, gt, gb, N, IN, OUT, c, workspace, sms, s);
+        if (rc != il::kNotApplicable) {
+            if (rc) {
+                cudaGetLastError();
+                return IL_ERR_LAUNCH;
+            }
+            return launch_status();
+        }
     }
     if (gx) {
         const unsigned g = grid_for(N * IN, 256, sms);

@@ -80,3 +80,17 @@ def normwise_close(got, ref, rtol: float, what: str = ""):
     worst = float((err / bound).max())
     assert worst <= 1.0, f"{what}: max err {err.max():.3e} exceeds rtol {rtol} (ratio {worst:.2f}, scale {scale:.3e})"
     return float(err.max() / max(scale, 1e-30))
+
+
+def same_bits(a, b) -> bool:
+    """Bitwise equality of fp32 arrays, with every NaN equal to every NaN
+    (the CPU propagates the input NaN's payload, the GPU returns the canonical
+    NaN; both are NaN in the reference's sense)."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    if a.shape != b.shape:
+        return False
+    na, nb = np.isnan(a), np.isnan(b)
+    if not np.array_equal(na, nb):
+        return False
+    return np.array_equal(a[~na].view(np.uint32), b[~nb].view(np.uint32))

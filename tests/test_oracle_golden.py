@@ -6,7 +6,7 @@ Bins are bit-exact; forward within 1e-5 and fp32 gradients within 1e-4
 import numpy as np
 import pytest
 
-from golden_io import bins_names, case_names, load_bins, load_case, normwise_close
+from golden_io import bins_names, case_names, load_bins, load_case, normwise_close, same_bits
 from oracle import oracle
 
 FWD_RTOL = 1e-5
@@ -21,8 +21,7 @@ def test_oracle_bins_bit_exact(name, dt):
     x = d[f"x_{dt}"]
     lo, _, fr = oracle.bins(x, d["K"], d["bw"], x_dtype=dt)
     assert np.array_equal(lo, d[f"lo_{dt}"])
-    # bit patterns (NaN-safe)
-    assert np.array_equal(fr.view(np.uint32), d[f"fr_{dt}"].view(np.uint32))
+    assert same_bits(fr, d[f"fr_{dt}"])
 
 
 @pytest.mark.parametrize("name", case_names())
@@ -31,7 +30,7 @@ def test_oracle_case(name):
     dt, K, bw = d["x_dtype"], d["K"], d["bw"]
     lo, hi, fr = oracle.bins(d["x"], K, bw, x_dtype=dt)
     assert np.array_equal(lo, d["lo"]) and np.array_equal(hi, d["hi"])
-    assert np.array_equal(fr.view(np.uint32), d["fr"].view(np.uint32))
+    assert same_bits(fr, d["fr"])
     out = oracle.forward(d["x"], d["table"], d["bias"], bw, x_dtype=dt)
     normwise_close(out, d["out"], FWD_RTOL, "out")
     gx, gt, gb = oracle.backward(d["go"], d["x"], d["table"], bw, x_dtype=dt)

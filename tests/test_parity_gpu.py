@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from golden_io import bins_names, case_names, load_bins, load_case, normwise_close
+from golden_io import bins_names, case_names, load_bins, load_case, normwise_close, same_bits
 from il_cases import CASES, EDGE_CASES, make_inputs, to_numpy_grad, x_numpy
 from oracle import oracle
 
@@ -53,7 +53,7 @@ def check_against_oracle(c, x, table, bias, go):
     lo, hi, fr = _lib.bins(x.to(DEV), c.K, bw)
     rlo, rhi, rfr = oracle.bins(xn, c.K, bw, x_dtype=c.dtype)
     assert np.array_equal(lo.cpu().numpy(), rlo) and np.array_equal(hi.cpu().numpy(), rhi)
-    assert np.array_equal(fr.cpu().numpy().view(np.uint32), rfr.view(np.uint32))
+    assert same_bits(fr.cpu().numpy(), rfr)
 
 
 @pytest.mark.parametrize("c", CASES + EDGE_CASES, ids=lambda c: c.name)
@@ -83,7 +83,7 @@ def test_bins_bit_exact_vs_golden(name, dt):
     x = _bf16_from_bits(xb) if dt == "bf16" else torch.from_numpy(xb)
     lo, hi, fr = _lib.bins(x.to(DEV), d["K"], d["bw"])
     assert np.array_equal(lo.cpu().numpy(), d[f"lo_{dt}"])
-    assert np.array_equal(fr.cpu().numpy().view(np.uint32), d[f"fr_{dt}"].view(np.uint32))
+    assert same_bits(fr.cpu().numpy(), d[f"fr_{dt}"])
 
 
 def test_forward_deterministic_and_token_independent():
