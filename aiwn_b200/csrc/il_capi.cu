@@ -154,7 +154,7 @@ int il_backward(const float* go, const void* x, int x_dtype, const float* table,
     if (gb && cudaMemsetAsync(gb, 0, (size_t)OUT * sizeof(float), s) != cudaSuccess)
         return IL_ERR_LAUNCH;
     if (N == 0) return IL_OK;
-    if (il::fast_backward_ok(go, x, x_dtype, table, gx, gt, gb, N, IN, OUT, K)) {
+    if (il::fast_backward_ok(go, x, x_dtype, table, gx, gt, gb, N, IN, OUT, K, c)) {
         const int rc =
             il::fast_backward(go, x, x_dtype, table, gx, gt, gb, N, IN, OUT, c, workspace, sms, s);
         if (rc != il::kNotApplicable) {

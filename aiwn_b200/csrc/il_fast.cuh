@@ -130,8 +130,14 @@ struct FwdArgs {
 
 constexpr int kFwdThreads = 1024;
 constexpr int kWarps = kFwdThreads / 32;
-constexpr int kSlots = 2;   // token slots per lane
-constexpr int kXB = 8;      // input columns whose x values a lane holds at once
+#ifndef IL_FWD_SLOTS
+#define IL_FWD_SLOTS 2
+#endif
+#ifndef IL_FWD_XB
+#define IL_FWD_XB 8
+#endif
+constexpr int kSlots = IL_FWD_SLOTS;  // token slots per lane
+constexpr int kXB = IL_FWD_XB;        // input columns handled per weights pass
 
 template <int C>
 __host__ __device__ constexpr int fwd_tile_tokens() {
@@ -573,6 +579,24 @@ inline int fast_forward(const void* x, int x_dtype, const float* table, const fl
 //   dtable: red.global.add.v4 of x*(1-fr)*go_jc into gt[lo, i, jc] and of
 //           x*fr*go_jc into gt[lo+1, i, jc] (gt zeroed beforehand).
 //   dbias:  CTAs of the first column group add up go over their tokens.
+// exact bins for bw = 2^-e (see gather_weights): lo, clamped fr and the
+// unclamped fr that decides whether the clamp passes the gradient
+template <int DT>
+__device__ __forceinline__ void bwd_bin(float xv, const BinCfg& c, int& lo, float& fr, float& frp) {
+    float q;
+    if constexpr (DT == kBF16) {
+        q = bf16_round(__fmul_rn(bf16_round(__fadd_rn(xv, 1.0f)), c.inv));
+    } else {
+        q = __fmaf_rn(xv, c.inv, c.inv);
+    }
+    float t = fminf(fmaxf(truncf(q), 0.0f), (float)(c.K - 1));
+    if (!(fabsf(q) < 9.2233720368547758e18f)) t = 0.0f;
+    frp = __fmul_rn(__fsub_rn(xv, __fmaf_rn(t, c.bw, -1.0f)), c.inv);
+    const float f = fminf(fmaxf(frp, 0.0f), 1.0f);
+    fr = (frp != frp) ? frp : f;
+    lo = (int)t;
+}
+
 template <int C>
 struct PairMap {
     static constexpr int G = C >= 32 ? 32 : (C > 16 ? 32 : (C > 8 ? 16 : (C > 4 ? 8 : (C > 2 ? 4 : (C > 1 ? 2 : 1)))));
@@ -657,7 +681,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
     }
     __syncthreads();
-    if (ig > 0 && (p.want_gx || p.want_gt)) mbar_wait_bounded(bar_s, 0);
+    if (ig > 0 && (p.want_gx || p.want_gt)) {
+        mbar_wait_bounded(bar_s, 0);
+        // row K of every slice = row K-1 (the reference's hi for the top bin)
+        for (int e = threadIdx.x; e < ig * C; e += kBwdThreads) {
+            const int s = e / C, c4 = e - s * C;
+            const uint32_t sl = table_s + (uint32_t)(s * p.slice_bytes);
+            sts_v4(sl + (uint32_t)(p.K * OUT * 4 + c4 * 16), lds_v4(sl + (uint32_t)((p.K - 1) * OUT * 4 + c4 * 16)));
+        }
+        __syncthreads();
+    }
 
     const int tg = lane / G, gl = lane % G;  // token in warp, lane in group
     const int row_stride = OUT * 4;
@@ -687,33 +720,61 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (!(p.want_gx || p.want_gt)) continue;
         const int64_t xrow = (int64_t)(tok ? n : 0) * p.IN + i0;
         for (int sb = 0; sb < ig; sb += kBwdV) {
+            // weights of the warp's (token, column) pairs, one lane per pair:
+            // pair j = s*P + token (s < kBwdV), held by lane j % 32 in register j / 32
+            constexpr int kNR = (kBwdV * P + 31) / 32;
+            uint32_t woff[kNR];
+            float w0[kNR], w1[kNR], wa_[kNR], wc_[kNR];
+#pragma unroll
+            for (int r = 0; r < kNR; ++r) {
+                const int j = r * 32 + lane;
+                const int s = j / P, tt = j - s * P;
+                const int nn = tile * TT + warp * P + tt;
+                const bool ok = s < kBwdV && sb + s < ig && nn < p.N;
+                const float xv = ok ? load_x<DT>(p.x, (int64_t)nn * p.IN + i0 + sb + s) : 0.0f;
+                int lo;
+                float fr, frp;
+                bwd_bin<DT>(xv, p.cfg, lo, fr, frp);
+                const float omf = __fsub_rn(1.0f, fr);
+                const float sl = clamp_passes(frp) ? __fmul_rn(xv, p.cfg.inv) : 0.0f;
+                woff[r] = (uint32_t)lo * row_stride;
+                w0[r] = omf - sl;
+                w1[r] = fr + sl;
+                wa_[r] = omf == 0.0f ? 0.0f : __fmul_rn(xv, omf);
+                wc_[r] = fr == 0.0f ? 0.0f : __fmul_rn(xv, fr);
+            }
             float part[kBwdV];
 #pragma unroll
             for (int k = 0; k < kBwdV; ++k) {
                 part[k] = 0.f;
-                const int s = sb + k;
-                if (!tok || s >= ig) continue;
-                const Bin b = bin_of<DT>(load_x<DT>(p.x, xrow + s), p.cfg);
-                const int hi = min(b.lo + 1, p.K - 1);
-                const uint32_t base = table_s + s * p.slice_bytes;
-                const float omf = __fsub_rn(1.0f, b.fr);
-                const float sl = clamp_passes(b.fr_pre) ? div_bw(b.x, p.cfg) : 0.0f;
-                const float wlo = omf - sl, whi = b.fr + sl;
-                const float wa = __fmul_rn(b.x, omf), wc = __fmul_rn(b.x, b.fr);
-                const int i = i0 + s;
+                const int j = k * P + tg;
+                const int r = (k * P) / 32;  // all P pairs of step k share one register
+                const uint32_t off = __shfl_sync(0xffffffffu, woff[r], j & 31);
+                const float a0 = __shfl_sync(0xffffffffu, w0[r], j & 31);
+                const float a1 = __shfl_sync(0xffffffffu, w1[r], j & 31);
+                float wa = 0.f, wc = 0.f;
+                if (p.want_gt) {
+                    wa = __shfl_sync(0xffffffffu, wa_[r], j & 31);
+                    wc = __shfl_sync(0xffffffffu, wc_[r], j & 31);
+                }
+                if (!tok || sb + k >= ig) continue;
+                const uint32_t base = table_s + (uint32_t)((sb + k) * p.slice_bytes) + off;
+                const int i = i0 + sb + k;
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
                     if (!cact[u]) continue;
                     const int jc = gl + G * u;
                     if (p.want_gx) {
-                        const float4 tl = lds_v4(base + b.lo * row_stride + jc * 16);
-                        const float4 th = lds_v4(base + hi * row_stride + jc * 16);
+                        const float4 tl = lds_v4(base + jc * 16);
+                        const float4 th = lds_v4(base + row_stride + jc * 16);
                         const float dl = gv[u].x * tl.x + gv[u].y * tl.y + gv[u].z * tl.z + gv[u].w * tl.w;
                         const float dh = gv[u].x * th.x + gv[u].y * th.y + gv[u].z * th.z + gv[u].w * th.w;
-                        part[k] += wlo * dl + whi * dh;
+                        part[k] += a0 * dl + a1 * dh;
                     }
                     if (p.want_gt) {
-                        float* rl = p.gt + ((int64_t)b.lo * p.IN + i) * OUT + 4 * jc;
+                        const int lo = (int)(off / row_stride);
+                        const int hi = min(lo + 1, p.K - 1);
+                        float* rl = p.gt + ((int64_t)lo * p.IN + i) * OUT + 4 * jc;
                         float* rh = p.gt + ((int64_t)hi * p.IN + i) * OUT + 4 * jc;
                         red_global_add_v4(rl, make_float4(wa * gv[u].x, wa * gv[u].y, wa * gv[u].z, wa * gv[u].w));
                         red_global_add_v4(rh, make_float4(wc * gv[u].x, wc * gv[u].y, wc * gv[u].z, wc * gv[u].w));
@@ -782,7 +843,7 @@ inline bool plan_backward(int K, int IN, int OUT, BwdPlan& pl) {
     const int m = 32 / std::gcd(OUT, 32);
     const int KB = round_up(ceil_div(K, nb), m);
     if (KB > 256) return false;
-    const int slice = KB * nb * OUT * 4;
+    const int slice = round_up(std::max(KB * nb, K + 1) * OUT * 4, 128);  // + row K
     const int fixed = 128 + 16 + OUT * 4 + 16;
     int IG = (kSmemBudget - fixed) / slice;
     if (IG < 1) return false;
@@ -797,7 +858,8 @@ inline int64_t fast_backward_workspace(int64_t, int64_t, int64_t, int64_t, int) 
 
 inline bool fast_backward_ok(const float* go, const void* x, int x_dtype, const float* table,
                              const void* gx, const float* gt, const float* gb, int64_t N, int64_t IN,
-                             int64_t OUT, int64_t K) {
+                             int64_t OUT, int64_t K, const BinCfg& c) {
+    if (!c.pow2) return false;  // the gathers' bucketing is written for bw = 2^-e
     if (N > ((int64_t)1 << 30) || IN > 65535 || K > 65535) return false;
     if (((uintptr_t)go | (uintptr_t)table | (uintptr_t)gt | (uintptr_t)gb) & 15) return false;
     if (x_dtype == kBF16 ? (((uintptr_t)x | (uintptr_t)gx) & 1) : (((uintptr_t)x | (uintptr_t)gx) & 3))
@@ -863,7 +925,9 @@ inline bool plan_dtable(int N, int K, int IN, int OUT, int sms, DtPlan& pl) {
     const int per = ceil_div(ceil_div(N, R), (int)tt) * (int)tt;
     R = ceil_div(N, per);
     pl = {C, (int)tt, R, per, (int)(fixed + per_tok * tt)};
-    return true;
+    // worth it only when a tile gives every row many contributions to add up in
+    // registers; sparse rows (large K) go to the gather kernel's vector reds
+    return 2 * tt >= 16 * (int64_t)(K + 1);
 }
 
 template <int DT, int C>
