@@ -209,6 +209,26 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int cid = CS > 1 ? (int)cluster_id_x() : (int)blockIdx.x;
     const int ncl = CS > 1 ? (int)nclusters_x() : (int)gridDim.x;
 
+    constexpr int XB = M::P >= 8 ? 2 : kXB;                // columns per weights pass
+    constexpr int kSpr = 16 / M::P;                        // steps per weight register
+    constexpr int kNR = (kSlots * XB + kSpr - 1) / kSpr;   // weight registers per block
+    const int pj = lane >> 1, pv = lane & 1;               // pair of this lane, lo/hi view
+    const int pt = pj % M::P, pst = pj / M::P;             // its token, step in register
+    // x values of the pairs this lane computes weights for, block (t, sb)
+    auto load_block_x = [&](int t, int sb_, float (&dst)[kNR]) {
+        const int nq_ = min(XB, ig - sb_);
+#pragma unroll
+        for (int r = 0; r < kNR; ++r) {
+            const int st = r * kSpr + pst;
+            const int q = st / kSlots, sl = st - q * kSlots;
+            const int n = t * TT + sl * (M::P * kWarps) + warp * M::P + pt;
+            const bool ok = t < p.ntiles && pj < kSpr * M::P && q < nq_ && n < p.N;
+            dst[r] = ok ? load_x<DT>(p.x, (int64_t)n * p.IN + i0 + sb_ + q) : 0.0f;
+        }
+    };
+    float xpre[kNR];
+    load_block_x(cid, 0, xpre);
+
     int k = 0;
     for (int tile = cid; tile < p.ntiles; tile += ncl, ++k) {
         float4 acc[kSlots][M::U];
@@ -223,29 +243,33 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         // lane 2j holds (byte offset of row lo, x(1-fr)), lane 2j+1 holds
         // (byte offset of row lo+1, x fr) of pair j.  Pair j of register r
         // is step st = r*kSpr + j/P (st = q*kSlots + slot) of token j%P.
-        constexpr int kSpr = 16 / M::P;                                   // steps per register
-        constexpr int kNR = (kSlots * kXB + kSpr - 1) / kSpr;             // registers per block
-        const int pj = lane >> 1, pv = lane & 1;
-        const int pt = pj % M::P, pst = pj / M::P;                        // token, step in register
-        for (int sb = 0; sb < ig; sb += kXB) {
-            const int nq = min(kXB, ig - sb);
+        // The x values of the next block (possibly of the next tile) are
+        // loaded before this block's gather, so their latency is hidden.
+        for (int sb = 0; sb < ig; sb += XB) {
+            const int nq = min(XB, ig - sb);
+            float xv[kNR];
+#pragma unroll
+            for (int r = 0; r < kNR; ++r) xv[r] = xpre[r];
+            {  // prefetch the following block
+                int nsb = sb + XB, ntile = tile;
+                if (nsb >= ig) {
+                    nsb = 0;
+                    ntile = tile + ncl;
+                }
+                load_block_x(ntile, nsb, xpre);
+            }
             uint32_t woff[kNR];
             float ww[kNR];
 #pragma unroll
             for (int r = 0; r < kNR; ++r) {
-                const int st = r * kSpr + pst;
-                const int q = st / kSlots, sl = st - q * kSlots;
-                const int n = tile * TT + sl * (M::P * kWarps) + warp * M::P + pt;
-                const bool ok = pj < kSpr * M::P && q < nq && n < p.N;
-                const float xv = ok ? load_x<DT>(p.x, (int64_t)n * p.IN + i0 + sb + q) : 0.0f;
                 int lo;
                 float wa, wc;
-                gather_weights<DT>(xv, p.cfg, lo, wa, wc);
+                gather_weights<DT>(xv[r], p.cfg, lo, wa, wc);
                 woff[r] = (uint32_t)(lo + pv) * row_stride;
                 ww[r] = pv ? wc : wa;
             }
 #pragma unroll
-            for (int q = 0; q < kXB; ++q) {
+            for (int q = 0; q < XB; ++q) {
                 if (q >= nq) break;
                 const uint32_t slice = table_s + (uint32_t)((sb + q) * p.slice_bytes);
 #pragma unroll
