@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <atomic>
@@ -15,6 +16,8 @@
 #include "il_common.cuh"
 #include "il_simple.cuh"
 #include "il_fast.cuh"
+#include "il_sorted.cuh"
+#include "il_fwd_token.cuh"
 
 namespace {
 
@@ -64,11 +67,29 @@ int check_common(const void* x, int x_dtype, int64_t N, int64_t IN, int64_t K, d
     return IL_OK;
 }
 
+// Kernel families.  AIWN_IL_FORWARD=token|cluster and AIWN_IL_BACKWARD=sorted|gather
+// restrict il_forward / il_backward to the named family (shapes it cannot take
+// fall through to the general kernels).  Unset, or any other value, selects
+// automatically: forward with one token per lane when every input column's
+// table slice fits one CTA, else the cluster kernel; backward by the bin-sorted
+// walk whenever the table gradient is wanted and the shape has a plan, else the
+// gather kernel.  The families compute the same results; the switches let the
+// tests cover each of them.
+enum KernelChoice { kAny = 0, kOnlyPreferred = 1, kOnlyOther = 2 };
+
+KernelChoice kernel_choice(const char* var, const char* preferred, const char* other) {
+    const char* v = getenv(var);
+    if (!v) return kAny;
+    if (strcmp(v, preferred) == 0) return kOnlyPreferred;
+    if (strcmp(v, other) == 0) return kOnlyOther;
+    return kAny;
+}
+
 std::atomic<int64_t> g_launches{0};
 
 // every kernel launch of the library is followed by this check
-inline int launch_status() {
-    g_launches.fetch_add(1, std::memory_order_relaxed);
+inline int launch_status(int kernels = 1) {
+    g_launches.fetch_add(kernels, std::memory_order_relaxed);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? IL_OK : IL_ERR_LAUNCH;
 }
@@ -113,7 +134,18 @@ int il_forward(const void* x, int x_dtype, const float* table, const float* bias
     if ((st = check_device(&sms))) return st;
     cudaStream_t s = (cudaStream_t)stream;
     const il::BinCfg c = make_cfg(bw, K);
-    if (il::fast_forward_ok(x, x_dtype, table, bias, out, N, IN, OUT, K, c)) {
+    const KernelChoice path = kernel_choice("AIWN_IL_FORWARD", "token", "cluster");
+    if (path != kOnlyOther && il::fast_forward_ok(x, x_dtype, table, bias, out, N, IN, OUT, K, c)) {
+        const int rc = il::token_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s);
+        if (rc != il::kNotApplicable) {
+            if (rc) {
+                cudaGetLastError();
+                return IL_ERR_LAUNCH;
+            }
+            return launch_status();
+        }
+    }
+    if (path != kOnlyPreferred && il::fast_forward_ok(x, x_dtype, table, bias, out, N, IN, OUT, K, c)) {
         const int rc = il::fast_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s);
         if (rc != il::kNotApplicable) {
             if (rc) {
@@ -154,15 +186,28 @@ int il_backward(const float* go, const void* x, int x_dtype, const float* table,
     if (gb && cudaMemsetAsync(gb, 0, (size_t)OUT * sizeof(float), s) != cudaSuccess)
         return IL_ERR_LAUNCH;
     if (N == 0) return IL_OK;
-    if (il::fast_backward_ok(go, x, x_dtype, table, gx, gt, gb, N, IN, OUT, K, c)) {
-        const int rc =
-            il::fast_backward(go, x, x_dtype, table, gx, gt, gb, N, IN, OUT, c, workspace, sms, s);
+    const KernelChoice path = kernel_choice("AIWN_IL_BACKWARD", "sorted", "gather");
+    if (path != kOnlyOther &&
+        il::sorted_backward_ok(go, x, x_dtype, table, gx, gt, gb, N, IN, OUT, K, c)) {
+        const int rc = il::sorted_backward(go, x, x_dtype, table, gx, gt, gb, N, IN, OUT, c, sms, s);
         if (rc != il::kNotApplicable) {
             if (rc) {
                 cudaGetLastError();
                 return IL_ERR_LAUNCH;
             }
             return launch_status();
+        }
+    }
+    if (path != kOnlyPreferred && il::fast_backward_ok(go, x, x_dtype, table, gx, gt, gb, N, IN, OUT, K, c)) {
+        int kernels = 0;
+        const int rc = il::fast_backward(go, x, x_dtype, table, gx, gt, gb, N, IN, OUT, c, workspace, sms, s,
+                                         &kernels);
+        if (rc != il::kNotApplicable) {
+            if (rc) {
+                cudaGetLastError();
+                return IL_ERR_LAUNCH;
+            }
+            return launch_status(kernels);
         }
     }
     if (gx) {

@@ -11,23 +11,20 @@
 //
 //   per tile of TT tokens
 //     1. bucket every token (bit-exact bins), count tokens per bin
-//     2. exclusive scan of the bin counts, scatter of (token, weights) into
-//        bin order (the order inside a bin follows shared-memory atomics, so
-//        the fp32 sums are not bitwise reproducible run to run; they agree
-//        with the reference to ~1e-6 relative)
-//     3. the "visit sequence" lists, row by row, the tokens contributing to
-//        row k: bin k's tokens (weight x(1-fr)) then bin k-1's (weight x fr).
-//        It is cut into equal pieces, one per lane group; a group walks its
-//        piece, accumulates go[token, 4jc:4jc+4] * weight in registers and
-//        adds the finished row into the CTA's gt slice in shared memory
-//        (plain read-modify-write: interior rows of a piece belong to that
-//        group alone; the first and last row of a piece may be shared with a
-//        neighbour group and use shared-memory atomics).
+//     2. exclusive scan of the bin counts, scatter of (token, weights, bin)
+//        into bin order (the order inside a bin follows shared-memory
+//        atomics, so the fp32 sums are not bitwise reproducible run to run;
+//        they agree with the reference to ~1e-6 relative)
+//     3. the sorted entries are cut into equal slices, one per lane group
+//        (C lanes, one 16-byte chunk of a row each).  A group walks its
+//        slice in order with two register accumulators: x(1-fr)*go for row
+//        `bin` and x*fr*go for row bin+1 (row K-1 for the top bin).  When the
+//        bin changes both are added into the CTA's gt slice in shared memory:
+//        plainly for bins inside the slice, with shared-memory atomics for
+//        the first and last bin (a neighbour group may hold part of them).
+//        go rows are read straight from global memory (L2), each row once
+//        per (token, column), with kDtDepth rows in flight per group.
 //   at the end the CTA adds its gt slice to global memory (vector reds).
-//
-// The top bin's hi contribution (lo = K-1, hi = K-1) is collected as a
-// virtual row K and folded into row K-1.  go tiles are double-buffered with
-// bulk copies so that loading tile t+1 overlaps the work on tile t.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -49,7 +46,7 @@ struct DtArgs {
     BinCfg cfg;
 };
 
-constexpr int kDtThreads = 1024;
+constexpr int kDtThreads = 512;
 
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
     asm volatile(
@@ -58,11 +55,13 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
         : "memory");
 }
 
-// block-wide exclusive scan of cnt[0..n) into out[0..n], out[n] = total
-// (n <= kDtThreads * 4; uses `tmp` of kDtThreads/32 ints)
+// block-wide exclusive scan of cnt[0..n) into out[0..n], out[n] = total, by
+// a block of NT threads (uses `tmp` of NT/32 <= 32 ints)
+template <int NT = kDtThreads>
 __device__ __forceinline__ void block_exclusive_scan(const uint32_t* cnt, uint32_t* out, int n,
                                                      uint32_t* tmp) {
-    const int per = (n + kDtThreads - 1) / kDtThreads;  // items per thread
+    static_assert(NT % 32 == 0 && NT <= 1024, "whole warps, at most 32 of them");
+    const int per = (n + NT - 1) / NT;  // items per thread
     const int b = threadIdx.x * per;
     uint32_t local = 0;
     for (int q = 0; q < per; ++q)
@@ -78,13 +77,13 @@ __device__ __forceinline__ void block_exclusive_scan(const uint32_t* cnt, uint32
     if (lane == 31) tmp[warp] = v;
     __syncthreads();
     if (warp == 0) {
-        uint32_t w = lane < kDtThreads / 32 ? tmp[lane] : 0;
+        uint32_t w = lane < NT / 32 ? tmp[lane] : 0;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const uint32_t t = __shfl_up_sync(0xffffffffu, w, o);
             if (lane >= o) w += t;
         }
-        if (lane < kDtThreads / 32) tmp[lane] = w;  // inclusive warp totals
+        if (lane < NT / 32) tmp[lane] = w;  // inclusive warp totals
     }
     __syncthreads();
     uint32_t run = (warp > 0 ? tmp[warp - 1] : 0) + v - local;
@@ -94,23 +93,42 @@ __device__ __forceinline__ void block_exclusive_scan(const uint32_t* cnt, uint32
             run += cnt[b + q];
         }
     }
-    if (threadIdx.x == kDtThreads - 1) out[n] = tmp[kDtThreads / 32 - 1];
+    if (threadIdx.x == NT - 1) out[n] = tmp[NT / 32 - 1];
 }
 
 template <int C>
 struct DtGroup {
     static_assert(C >= 1 && C <= 32, "a row is covered by one group of at most 32 lanes");
-    static constexpr int G = C;                              // lanes per row group (one chunk each)
+    static constexpr int G = C;                              // lanes per group (one chunk each)
     static constexpr int GPW = 32 / C;                       // groups per warp
     static constexpr int NG = GPW * (kDtThreads / 32);       // groups per CTA
 };
 
-// per sorted entry: token (as bits), x(1-fr), x*fr
+// sorted entry: token (offset in the tile), x(1-fr), x*fr, bin
 struct __align__(16) DtEntry {
     uint32_t tok;
     float wa, wc;
-    uint32_t pad;
+    uint32_t bin;
 };
+
+constexpr int kDtDepth = 6;  // entries whose go rows are in flight per group
+
+__device__ __forceinline__ void flush_row(float* gts, int OUT, int row, int gl, float4 a, bool shared) {
+    float* d = gts + (size_t)row * OUT + 4 * gl;
+    if (shared) {
+        atomicAdd(d + 0, a.x);
+        atomicAdd(d + 1, a.y);
+        atomicAdd(d + 2, a.z);
+        atomicAdd(d + 3, a.w);
+    } else {
+        float4 o = *reinterpret_cast<float4*>(d);
+        o.x += a.x;
+        o.y += a.y;
+        o.z += a.z;
+        o.w += a.w;
+        *reinterpret_cast<float4*>(d) = o;
+    }
+}
 
 template <int DT, int C>
 __global__ void __launch_bounds__(kDtThreads, 1) dtable_kernel(const DtArgs p) {
@@ -128,160 +146,99 @@ __global__ void __launch_bounds__(kDtThreads, 1) dtable_kernel(const DtArgs p) {
     // shared memory layout (from a 128-byte aligned base)
     const uint32_t base = (smem_addr(smem) + 127u) & ~127u;
     unsigned char* gen = smem + (base - smem_addr(smem));
-    const uint32_t go_bytes = (uint32_t)(TT * OUT * 4);
-    const uint32_t go_s0 = base, go_s1 = base + go_bytes;        // go tiles (double buffer)
-    DtEntry* ent = reinterpret_cast<DtEntry*>(gen + 2 * go_bytes);    // sorted entries [TT]
-    DtEntry* tke = ent + TT;                                          // per token [TT] (tok = bin)
-    float* gts = reinterpret_cast<float*>(tke + TT);                  // gt slice [(K+1)][OUT]
-    uint32_t* cnt = reinterpret_cast<uint32_t*>(gts + (size_t)(K + 1) * OUT);  // [K+1]
+    DtEntry* ent = reinterpret_cast<DtEntry*>(gen);                   // sorted entries [TT]
+    DtEntry* tke = ent + TT;                                          // per token [TT]
+    float* gts = reinterpret_cast<float*>(tke + TT);                  // gt slice [K][OUT]
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(gts + (size_t)K * OUT);  // [K+1]
     uint32_t* sb = cnt + (K + 1);                                     // bin starts [K+1]
     uint32_t* tmp = sb + (K + 1);                                     // scan scratch [32]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uintptr_t>(tmp + 32 + 1) & ~uintptr_t(7));
-    const uint32_t bar0 = smem_addr(bars), bar1 = bar0 + 8;
 
-    for (int e = threadIdx.x; e < (K + 1) * OUT; e += kDtThreads) gts[e] = 0.f;
+    for (int e = threadIdx.x; e < K * OUT; e += kDtThreads) gts[e] = 0.f;
     for (int e = threadIdx.x; e < K + 1; e += kDtThreads) cnt[e] = 0;
-    const int ntile = r1 > r0 ? (r1 - r0 + TT - 1) / TT : 0;
-    if (threadIdx.x == 0) {
-        mbar_init(bar0, 1);
-        mbar_init(bar1, 1);
-        fence_mbar_init();
-        fence_proxy_async_smem();
-        if (ntile > 0) {
-            const int nt = min(TT, r1 - r0);
-            mbar_arrive_expect_tx(bar0, (uint32_t)(nt * OUT * 4));
-            bulk_load(go_s0, p.go + (int64_t)r0 * OUT, (uint32_t)(nt * OUT * 4), bar0);
-        }
-    }
     __syncthreads();
 
-    float4 bsum = make_float4(0.f, 0.f, 0.f, 0.f);  // bias gradient (column i == 0 CTAs)
+    const int ntile = r1 > r0 ? (r1 - r0 + TT - 1) / TT : 0;
     for (int t = 0; t < ntile; ++t) {
         const int t0 = r0 + t * TT;
         const int nt = min(TT, r1 - t0);
-        const uint32_t go_s = (t & 1) ? go_s1 : go_s0;
-        const float* gos = reinterpret_cast<const float*>(gen + (go_s - base));
-        // prefetch the next tile into the other buffer (its last readers
-        // finished before the __syncthreads that closed tile t-1)
-        if (threadIdx.x == 0 && t + 1 < ntile) {
-            const int t1 = t0 + TT;
-            const int n1 = min(TT, r1 - t1);
-            const uint32_t bn = (t & 1) ? bar0 : bar1;
-            fence_proxy_async_smem();
-            mbar_arrive_expect_tx(bn, (uint32_t)(n1 * OUT * 4));
-            bulk_load((t & 1) ? go_s0 : go_s1, p.go + (int64_t)t1 * OUT, (uint32_t)(n1 * OUT * 4), bn);
-        }
         // 1. bins and weights of the tile's tokens; counts per bin
-        if (threadIdx.x < nt) {
-            const Bin b = bin_of<DT>(load_x<DT>(p.x, (int64_t)(t0 + threadIdx.x) * p.IN + i), p.cfg);
+        for (int tk = threadIdx.x; tk < nt; tk += kDtThreads) {
+            const Bin b = bin_of<DT>(load_x<DT>(p.x, (int64_t)(t0 + tk) * p.IN + i), p.cfg);
             DtEntry e;
-            e.tok = (uint32_t)b.lo;
+            e.tok = (uint32_t)tk;
             e.wa = __fmul_rn(b.x, __fsub_rn(1.0f, b.fr));
             e.wc = __fmul_rn(b.x, b.fr);
-            e.pad = 0;
-            tke[threadIdx.x] = e;
+            e.bin = (uint32_t)b.lo;
+            tke[tk] = e;
             atomicAdd(&cnt[b.lo], 1u);
         }
         __syncthreads();
-        // 2. bin starts (exclusive scan, sb[K] = nt), then scatter into bin order
+        // 2. bin starts (exclusive scan), then scatter into bin order
         block_exclusive_scan(cnt, sb, K, tmp);
         __syncthreads();
         for (int e = threadIdx.x; e < K + 1; e += kDtThreads) cnt[e] = 0;
         __syncthreads();
-        if (threadIdx.x < nt) {
-            DtEntry e = tke[threadIdx.x];
-            const uint32_t lo = e.tok;
-            const uint32_t pos = sb[lo] + atomicAdd(&cnt[lo], 1u);
-            e.tok = (uint32_t)threadIdx.x;
+        for (int tk = threadIdx.x; tk < nt; tk += kDtThreads) {
+            const DtEntry e = tke[tk];
+            const uint32_t pos = sb[e.bin] + atomicAdd(&cnt[e.bin], 1u);
             ent[pos] = e;
         }
-        // go tile t has landed (waited by everyone before reading it)
-        mbar_wait_bounded((t & 1) ? bar1 : bar0, (uint32_t)((t >> 1) & 1));
         __syncthreads();
-        // 3. walk the visit sequence: rows 0..K (row K = top bin's hi part).
-        //    V(k) = S(k) + S(k-1) visits precede row k (S = bin starts); 2*nt visits
-        const int total = 2 * nt;
-        const int per = (total + NG - 1) / NG;
-        const int v0 = glive ? min(total, grp * per) : total;
-        const int v1 = min(total, v0 + per);
-        if (v0 < v1) {
-            int k = 0;
-            {  // largest k in [0, K] with V(k) <= v0
-                int lo_k = 0, hi_k = K;
-                while (lo_k < hi_k) {
-                    const int mid = (lo_k + hi_k + 1) >> 1;
-                    if (sb[mid] + sb[mid - 1] <= (uint32_t)v0) lo_k = mid;
-                    else hi_k = mid - 1;
+        // 3. each group walks an equal slice of the sorted entries; row `bin`
+        //    gets x(1-fr) go, row bin+1 (K-1 for the top bin) gets x fr go
+        const int per = (nt + NG - 1) / NG;
+        const int e0 = glive ? min(nt, grp * per) : nt;
+        const int e1 = min(nt, e0 + per);
+        if (e0 < e1) {
+            const int bfirst = (int)ent[e0].bin, blast = (int)ent[e1 - 1].bin;
+            const float* gob = p.go + (int64_t)t0 * OUT + 4 * gl;
+            float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+            int cur = bfirst;
+            // prefetch the first kDtDepth entries' go chunks
+            DtEntry en[kDtDepth];
+            float4 gv[kDtDepth];
+#pragma unroll
+            for (int d = 0; d < kDtDepth; ++d) {
+                if (e0 + d < e1) {
+                    en[d] = ent[e0 + d];
+                    gv[d] = __ldg(reinterpret_cast<const float4*>(gob + (size_t)en[d].tok * OUT));
                 }
-                k = lo_k;
             }
-            // registers describing row k
-            uint32_t sbk = sb[k], sbp = k > 0 ? sb[k - 1] : 0u;
-            uint32_t sbn = k < K ? sb[k + 1] : sbk;
-            uint32_t vk = sbk + sbp;
-            uint32_t vsplit = vk + (k < K ? sbn - sbk : 0u);   // end of the lo part
-            uint32_t vnext = k < K ? sbn + sbk : (uint32_t)total;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            bool first = true, any = false;
-            for (uint32_t v = (uint32_t)v0; v < (uint32_t)v1; ++v) {
-                while (v >= vnext) {  // row k is complete
-                    if (any) {
-                        float* d = gts + (size_t)(k == K ? K - 1 : k) * OUT + 4 * gl;
-                        // rows another group may also add to: the first row of
-                        // this piece and rows K-1 / K (top bin)
-                        if (first || k >= K - 1) {
-                            atomicAdd(d + 0, acc.x);
-                            atomicAdd(d + 1, acc.y);
-                            atomicAdd(d + 2, acc.z);
-                            atomicAdd(d + 3, acc.w);
-                        } else {
-                            float4 o = *reinterpret_cast<float4*>(d);
-                            o.x += acc.x;
-                            o.y += acc.y;
-                            o.z += acc.z;
-                            o.w += acc.w;
-                            *reinterpret_cast<float4*>(d) = o;
-                        }
+            for (int e = e0; e < e1; e += kDtDepth) {
+#pragma unroll
+                for (int d = 0; d < kDtDepth; ++d) {
+                    if (e + d >= e1) break;
+                    const DtEntry c = en[d];
+                    const float4 g = gv[d];
+                    // refill this slot with the entry kDtDepth ahead
+                    const int nx = e + d + kDtDepth;
+                    if (nx < e1) {
+                        en[d] = ent[nx];
+                        gv[d] = __ldg(reinterpret_cast<const float4*>(gob + (size_t)en[d].tok * OUT));
                     }
-                    acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                    first = false;
-                    any = false;
-                    ++k;
-                    sbp = sbk;
-                    sbk = sbn;
-                    sbn = k < K ? sb[k + 1] : sbk;
-                    vk = vnext;
-                    vsplit = vk + (k < K ? sbn - sbk : 0u);
-                    vnext = k < K ? sbn + sbk : (uint32_t)total;
+                    if ((int)c.bin != cur) {
+                        // rows next to either end of the slice can also receive
+                        // a neighbour group's part of a split bin
+                        const int rh = min(cur + 1, K - 1);
+                        flush_row(gts, OUT, cur, gl, lo, cur <= bfirst + 1 || cur >= blast);
+                        flush_row(gts, OUT, rh, gl, hi, rh <= bfirst + 1 || rh >= blast);
+                        lo = make_float4(0.f, 0.f, 0.f, 0.f);
+                        hi = lo;
+                        cur = (int)c.bin;
+                    }
+                    lo.x = fmaf(c.wa, g.x, lo.x);
+                    lo.y = fmaf(c.wa, g.y, lo.y);
+                    lo.z = fmaf(c.wa, g.z, lo.z);
+                    lo.w = fmaf(c.wa, g.w, lo.w);
+                    hi.x = fmaf(c.wc, g.x, hi.x);
+                    hi.y = fmaf(c.wc, g.y, hi.y);
+                    hi.z = fmaf(c.wc, g.z, hi.z);
+                    hi.w = fmaf(c.wc, g.w, hi.w);
                 }
-                const bool lopart = v < vsplit;
-                const uint32_t e = lopart ? v - vk + sbk : v - vsplit + sbp;
-                const DtEntry en = ent[e];
-                const float w = lopart ? en.wa : en.wc;
-                const float4 g = *reinterpret_cast<const float4*>(gos + (size_t)en.tok * OUT + 4 * gl);
-                acc.x = fmaf(w, g.x, acc.x);
-                acc.y = fmaf(w, g.y, acc.y);
-                acc.z = fmaf(w, g.z, acc.z);
-                acc.w = fmaf(w, g.w, acc.w);
-                any = true;
             }
-            if (any) {  // last row of the piece (possibly shared with the next group)
-                float* d = gts + (size_t)(k == K ? K - 1 : k) * OUT + 4 * gl;
-                atomicAdd(d + 0, acc.x);
-                atomicAdd(d + 1, acc.y);
-                atomicAdd(d + 2, acc.z);
-                atomicAdd(d + 3, acc.w);
-            }
-        }
-        // bias gradient: CTAs of column 0 add up the tile's go rows
-        if (p.want_gb && i == 0 && glive) {
-            for (int tk = grp; tk < nt; tk += NG) {
-                const float4 g = *reinterpret_cast<const float4*>(gos + (size_t)tk * OUT + 4 * gl);
-                bsum.x += g.x;
-                bsum.y += g.y;
-                bsum.z += g.z;
-                bsum.w += g.w;
-            }
+            // the last bin of the slice may continue in the next group's slice
+            flush_row(gts, OUT, cur, gl, lo, true);
+            flush_row(gts, OUT, min(cur + 1, K - 1), gl, hi, true);
         }
         for (int e = threadIdx.x; e < K + 1; e += kDtThreads) cnt[e] = 0;
         __syncthreads();
@@ -291,13 +248,6 @@ __global__ void __launch_bounds__(kDtThreads, 1) dtable_kernel(const DtArgs p) {
         const int k = e / (OUT / 4), c4 = e - k * (OUT / 4);
         const float4 v = *reinterpret_cast<const float4*>(gts + (size_t)k * OUT + 4 * c4);
         red_global_add_v4(p.gt + ((int64_t)k * p.IN + i) * OUT + 4 * c4, v);
-    }
-    if (p.want_gb && i == 0 && glive) {
-        float* d = p.gb + 4 * gl;
-        atomicAdd(d + 0, bsum.x);
-        atomicAdd(d + 1, bsum.y);
-        atomicAdd(d + 2, bsum.z);
-        atomicAdd(d + 3, bsum.w);
     }
 }
 

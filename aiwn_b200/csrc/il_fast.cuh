@@ -120,6 +120,8 @@ struct FwdArgs {
     float* out;
     int N, IN, OUT, K;
     int JR;           // j-range width (floats) = 4*C
+    int RS;           // row stride of a table slice in shared memory (floats, >= JR)
+    int xvec;         // x rows can be read 4 elements at a time (aligned, IN % 4 == 0)
     int IG;           // input columns per CTA of a cluster
     int KB;           // rows per TMA box
     int nbox;         // boxes per slice
@@ -128,7 +130,10 @@ struct FwdArgs {
     BinCfg cfg;
 };
 
-constexpr int kFwdThreads = 1024;
+#ifndef IL_FWD_THREADS
+#define IL_FWD_THREADS 1024
+#endif
+constexpr int kFwdThreads = IL_FWD_THREADS;
 constexpr int kWarps = kFwdThreads / 32;
 #ifndef IL_FWD_SLOTS
 #define IL_FWD_SLOTS 2
@@ -355,8 +360,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             if (threadIdx.x == 0) mbar_arrive_expect_tx_local(bar_full, (uint32_t)(CS * TTQ * C * 16));
             const bool reducer = threadIdx.x < TTQ * C;
             if (reducer) mbar_wait_cluster_bounded(bar_full, (uint32_t)(k & 1));
-            if (reducer) {
-                const int e = threadIdx.x;
+            for (int e = threadIdx.x; e < TTQ * C; e += kFwdThreads) {
                 const int tq = e / C, jc = e - tq * C;
                 float4 s = lds_v4(recv_s + (uint32_t)((tq * C + jc) * 16));
 #pragma unroll
@@ -379,8 +383,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             }
             // 3) the receive buffer may be refilled once every reader is done
             //    (named barrier 1 over the reducer warps only)
-            constexpr int kRedThreads = ((TTQ * C + 31) / 32) * 32;
-            static_assert(kRedThreads <= kFwdThreads, "one item per reducer thread");
+            constexpr int kRedRounded = ((TTQ * C + 31) / 32) * 32;
+            constexpr int kRedThreads = kRedRounded < kFwdThreads ? kRedRounded : kFwdThreads;
             if (threadIdx.x < kRedThreads) {
                 asm volatile("bar.sync 1, %0;" ::"n"(kRedThreads) : "memory");
                 if (threadIdx.x < CS) mbar_arrive_remote(map_to_rank(bar_empty, (uint32_t)threadIdx.x));
@@ -429,7 +433,7 @@ inline bool make_table_map(CUtensorMap* m, const float* table, int K, int IN, in
 constexpr int kSmemBudget = 227 * 1024 - 1024;  // dynamic shared memory per CTA (static part aside)
 
 struct FwdPlan {
-    int C = 0, CS = 0, JR = 0, IG = 0, KB = 0, nbox = 0, slice_bytes = 0, smem = 0;
+    int C = 0, CS = 0, JR = 0, IG = 0, KB = 0, nbox = 0, slice_bytes = 0, smem = 0, RS = 0;
 };
 
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
@@ -578,6 +582,8 @@ inline int fast_forward(const void* x, int x_dtype, const float* table, const fl
     a.OUT = (int)OUT;
     a.K = c.K;
     a.JR = pl.JR;
+    a.RS = pl.JR;
+    a.xvec = 0;
     a.IG = pl.IG;
     a.KB = pl.KB;
     a.nbox = pl.nbox;
@@ -938,20 +944,23 @@ inline bool plan_dtable(int N, int K, int IN, int OUT, int sms, DtPlan& pl) {
     for (int c : kDtChunks) inst |= (c == C);
     if (!inst) return false;
     // bytes that do not scale with the tile: alignment, gt slice, bin counters,
-    // scan scratch, barriers (+ padding)
-    const int64_t fixed = 128 + (int64_t)(K + 1) * OUT * 4 + (int64_t)(2 * K + 2) * 4 + 33 * 4 + 8 + 16;
-    const int64_t per_tok = 2 * OUT * 4 + 2 * 16;  // go tiles (x2) + per-token and sorted entries
+    // scan scratch (+ padding)
+    const int64_t fixed = 128 + (int64_t)K * OUT * 4 + (int64_t)(2 * K + 2) * 4 + 33 * 4 + 16;
+    const int64_t per_tok = 2 * 16;  // per-token and sorted entries
     int64_t tt = (kSmemBudget - fixed) / per_tok;
-    tt = std::min<int64_t>(tt, kDtThreads) / 32 * 32;
+    tt = std::min<int64_t>(tt, 4096) / 32 * 32;
     if (tt < 32) return false;
     int R = std::max(1, sms / IN);
     R = std::min(R, ceil_div(N, (int)tt));
     const int per = ceil_div(ceil_div(N, R), (int)tt) * (int)tt;
     R = ceil_div(N, per);
     pl = {C, (int)tt, R, per, (int)(fixed + per_tok * tt)};
-    // worth it only when a tile gives every row many contributions to add up in
-    // registers; sparse rows (large K) go to the gather kernel's vector reds
-    return 2 * tt >= 16 * (int64_t)(K + 1);
+    // sorting pays off only when a tile gives each row many contributions
+    // (>= 64 per tile on average: K <= 64 at 4096 tokens).  Measured on B200:
+    // at K=512 (4 per row per 1024 tokens) the vector reductions of the gather
+    // kernel win (120 us vs 181 us for sort + separate dx), at K=128 they tie
+    // or win, at K=16 the two are equal.
+    return tt >= 64 * (int64_t)K;
 }
 
 template <int DT, int C>
@@ -982,13 +991,14 @@ inline int launch_dtable_c(const DtArgs& a, const DtPlan& pl, cudaStream_t s) {
 // gather kernel also scatters gt with vector reductions.
 inline int fast_backward(const float* go, const void* x, int x_dtype, const float* table, void* gx,
                          float* gt, float* gb, int64_t N, int64_t IN, int64_t OUT, const BinCfg& c,
-                         void*, int sms, cudaStream_t s) {
+                         void*, int sms, cudaStream_t s, int* kernels) {
+    *kernels = 0;
     BwdPlan pl;
     if (!plan_backward(c.K, (int)IN, (int)OUT, pl)) return kNotApplicable;
     DtPlan dp;
     const bool dt_ok = gt != nullptr && plan_dtable((int)N, c.K, (int)IN, (int)OUT, sms, dp);
     int rc = 0;
-    if (gx || (!dt_ok && (gt || gb))) {
+    if (gx || gb || (!dt_ok && gt)) {
         CUtensorMap map;
         if (!make_table_map(&map, table, c.K, (int)IN, (int)OUT, (int)OUT, pl.KB)) return kNotApplicable;
         BwdArgs a;
@@ -1008,10 +1018,11 @@ inline int fast_backward(const float* go, const void* x, int x_dtype, const floa
         a.ntiles = ceil_div((int)N, bwd_tokens_per_tile(pl.C));
         a.want_gx = gx != nullptr;
         a.want_gt = !dt_ok && gt != nullptr;
-        a.want_gb = !dt_ok && gb != nullptr;
+        a.want_gb = gb != nullptr;
         a.cfg = c;
         rc = x_dtype == kBF16 ? launch_bwd_c<kBF16>(map, a, pl, sms, s) : launch_bwd_c<kF32>(map, a, pl, sms, s);
         if (rc) return rc;
+        *kernels = 1;
         if (!dt_ok) return 0;
         if (cudaGetLastError() != cudaSuccess) return 4;
     }
@@ -1026,8 +1037,9 @@ inline int fast_backward(const float* go, const void* x, int x_dtype, const floa
     d.K = c.K;
     d.TT = dp.TT;
     d.tok_per_cta = dp.tok_per_cta;
-    d.want_gb = gb != nullptr;
+    d.want_gb = 0;
     d.cfg = c;
+    *kernels += 1;
     return x_dtype == kBF16 ? launch_dtable_c<kBF16>(d, dp, s) : launch_dtable_c<kF32>(d, dp, s);
 }
 

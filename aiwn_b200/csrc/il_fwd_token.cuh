@@ -1,0 +1,233 @@
+// il_fwd_token.cuh -- IndexedLinear forward with one token per lane.
+//
+//   out[n, j0:j0+JR] = bias + sum_i  x(1-fr) T[lo,i,j0:j0+JR] + x fr T[lo+1,i,j0:j0+JR]
+//
+// (aiwn/layers/indexed_linear.py:173-182; bins bit-exact as in
+// gather_weights).  A CTA owns one j-range of JR = 4*C output columns and
+// keeps the slices T[:, i, j0:j0+JR] of ALL input columns resident in shared
+// memory (TMA tensor copies, one extra row K = row K-1 per slice so that row
+// lo+1 always exists).  Each lane then handles one token on its own: it
+// computes the bins of its token's x values and reads the 2*C 16-byte chunks
+// of rows lo and lo+1 with 128-bit shared loads, accumulating JR outputs in
+// registers.  Nothing is exchanged between lanes or CTAs; the price is that
+// the OUT/JR CTAs of a token range each bin the token's x values.
+//
+// Shared-memory gathers from 32 random rows per warp instruction need ~7.4
+// wavefronts for 32 chunks (4 when conflict-free): that, not HBM, bounds the
+// kernel.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "il_common.cuh"
+#include "il_fast.cuh"
+#include "il_sm100.cuh"
+
+namespace il {
+
+constexpr int kTokXB = 4;  // input columns per x block (prefetched one block ahead)
+
+// threads per CTA (one token each): more warps hide latency where the
+// per-token state is small
+__host__ __device__ constexpr int tok_threads(int C) { return C <= 2 ? 1024 : 512; }
+
+// Each CTA owns the contiguous token range [blockIdx.x * p.ntiles, ...) of
+// p.ntiles tokens (here `ntiles` is the range length) and walks it in steps of
+// one token per thread, so that the work per SM is balanced to the token.
+template <int DT, int C>
+__global__ void __launch_bounds__(tok_threads(C), 1)
+    fwd_token_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs p) {
+    constexpr int kTokThreads = tok_threads(C);
+    extern __shared__ unsigned char smem[];
+    const int IN = p.IN;
+    const int j0 = blockIdx.y * p.JR;
+    const uint32_t table_s = (smem_addr(smem) + 127u) & ~127u;
+    const uint32_t bar = table_s + (uint32_t)(IN * p.slice_bytes);
+    const uint32_t row_bytes = (uint32_t)p.RS * 4;
+
+    if (threadIdx.x == 0) {
+        prefetch_tensormap(&tmap);
+        mbar_init(bar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(bar, (uint32_t)(IN * p.nbox * p.KB * p.RS * 4));
+        for (int s = 0; s < IN; ++s)
+            for (int b = 0; b < p.nbox; ++b)
+                tma_load_3d(table_s + s * p.slice_bytes + b * p.KB * p.RS * 4, &tmap, bar, j0, s, b * p.KB);
+    }
+    __syncthreads();
+    mbar_wait_bounded(bar, 0);
+    for (int e = threadIdx.x; e < IN * C; e += kTokThreads) {
+        const int s = e / C, c4 = e - s * C;
+        const uint32_t sl = table_s + (uint32_t)(s * p.slice_bytes);
+        sts_v4(sl + (uint32_t)p.K * row_bytes + c4 * 16, lds_v4(sl + (uint32_t)(p.K - 1) * row_bytes + c4 * 16));
+    }
+    __syncthreads();
+
+    const int r0 = blockIdx.x * p.ntiles;
+    const int r1 = min(p.N, r0 + p.ntiles);
+    // x values of block (token n, columns [sb, sb+kTokXB))
+    static_assert(kTokXB == 4, "vector x loads read 4 elements");
+    auto load_block = [&](int n, int sb, float (&dst)[kTokXB]) {
+        const bool ok = n < r1;
+        const int64_t at = (int64_t)n * IN + sb;
+        if (p.xvec) {  // one 16-byte (fp32) or 8-byte (bf16) load
+            if constexpr (DT == kBF16) {
+                uint2 v = ok ? __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p.x) + at))
+                             : make_uint2(0u, 0u);
+                dst[0] = __uint_as_float(v.x << 16);
+                dst[1] = __uint_as_float(v.x & 0xffff0000u);
+                dst[2] = __uint_as_float(v.y << 16);
+                dst[3] = __uint_as_float(v.y & 0xffff0000u);
+            } else {
+                const float4 v = ok ? __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + at))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+                dst[0] = v.x;
+                dst[1] = v.y;
+                dst[2] = v.z;
+                dst[3] = v.w;
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < kTokXB; ++q) dst[q] = (ok && sb + q < IN) ? load_x<DT>(p.x, at + q) : 0.0f;
+        }
+    };
+    float xpre[kTokXB];
+    load_block(r0 + (int)threadIdx.x, 0, xpre);
+
+    for (int n = r0 + (int)threadIdx.x; n - (int)threadIdx.x < r1; n += kTokThreads) {
+        float4 acc[C];
+#pragma unroll
+        for (int c = 0; c < C; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int sb = 0; sb < IN; sb += kTokXB) {
+            float xv[kTokXB];
+#pragma unroll
+            for (int q = 0; q < kTokXB; ++q) xv[q] = xpre[q];
+            if (sb + kTokXB < IN) load_block(n, sb + kTokXB, xpre);
+            else load_block(n + kTokThreads, 0, xpre);
+#pragma unroll
+            for (int q = 0; q < kTokXB; ++q) {
+                if (sb + q >= IN) break;
+                int lo;
+                float wa, wc;
+                gather_weights<DT>(xv[q], p.cfg, lo, wa, wc);
+                const uint32_t row = table_s + (uint32_t)((sb + q) * p.slice_bytes) + (uint32_t)lo * row_bytes;
+#pragma unroll
+                for (int c = 0; c < C; ++c) {
+                    const float4 tl = lds_v4(row + c * 16);
+                    const float4 th = lds_v4(row + row_bytes + c * 16);
+                    acc[c].x = fmaf(wa, tl.x, acc[c].x);
+                    acc[c].y = fmaf(wa, tl.y, acc[c].y);
+                    acc[c].z = fmaf(wa, tl.z, acc[c].z);
+                    acc[c].w = fmaf(wa, tl.w, acc[c].w);
+                    acc[c].x = fmaf(wc, th.x, acc[c].x);
+                    acc[c].y = fmaf(wc, th.y, acc[c].y);
+                    acc[c].z = fmaf(wc, th.z, acc[c].z);
+                    acc[c].w = fmaf(wc, th.w, acc[c].w);
+                }
+            }
+        }
+        if (n < r1) {
+            float4* o = reinterpret_cast<float4*>(p.out + (int64_t)n * p.OUT + j0);
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+                const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + j0) + c);
+                o[c] = make_float4(acc[c].x + b.x, acc[c].y + b.y, acc[c].z + b.z, acc[c].w + b.w);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+constexpr int kTokChunks[] = {8, 5, 4, 2, 1};
+
+// j-range width: the widest whose slices of every input column fit one CTA's
+// shared memory, narrowed while the token ranges alone would leave SMs idle
+// (a narrower j-range gives more CTAs per token range)
+inline bool plan_token_forward(int64_t N, int K, int IN, int OUT, int sms, FwdPlan& pl) {
+    if (OUT % 4 != 0) return false;
+    const int chunks = OUT / 4;
+    bool found = false;
+    for (int C : kTokChunks) {
+        if (chunks % C != 0) continue;
+        const int JR = 4 * C;
+        const int RS = (C % 2 == 0) ? JR + 4 : JR;
+        const int nb = ceil_div(K, 256);
+        const int m = 32 / std::gcd(RS, 32);  // keeps every box 128-byte aligned
+        const int KB = round_up(ceil_div(K, nb), m);
+        if (KB > 256) continue;
+        const int slice = round_up(std::max(KB * nb, K + 1) * RS * 4, 128);
+        const int64_t smem = (int64_t)IN * slice + 128 + 16;  // + base alignment + mbarrier
+        if (smem > kSmemBudget) continue;
+        pl = {C, 1, JR, IN, KB, nb, slice, (int)smem};
+        pl.RS = RS;
+        found = true;
+        const int64_t ranges = (N + tok_threads(C) - 1) / tok_threads(C);
+        if (ranges * (chunks / C) >= sms) break;  // enough CTAs at this width
+    }
+    return found;
+}
+
+template <int DT, int C>
+inline int launch_token_fwd(const CUtensorMap& map, const FwdArgs& a, const FwdPlan& pl, int sms,
+                            cudaStream_t s) {
+    auto kern = fwd_token_kernel<DT, C>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem) != cudaSuccess)
+        return 4;
+    const int jranges = ceil_div(a.OUT, pl.JR);
+    const int T = tok_threads(C);
+    // contiguous token ranges, one per CTA, a multiple of 32 tokens each
+    const int max_ranges = std::max(1, sms / jranges);
+    int per = round_up(ceil_div(a.N, max_ranges), 32);
+    per = std::max(per, 32);
+    FwdArgs b = a;
+    b.ntiles = per;
+    const int ranges = ceil_div(a.N, per);
+    kern<<<dim3((unsigned)ranges, (unsigned)jranges, 1), T, pl.smem, s>>>(map, b);
+    (void)T;
+    return 0;
+}
+
+template <int DT>
+inline int launch_token_fwd_c(const CUtensorMap& map, const FwdArgs& a, const FwdPlan& pl, int sms,
+                              cudaStream_t s) {
+    switch (pl.C) {
+        case 8: return launch_token_fwd<DT, 8>(map, a, pl, sms, s);
+        case 5: return launch_token_fwd<DT, 5>(map, a, pl, sms, s);
+        case 4: return launch_token_fwd<DT, 4>(map, a, pl, sms, s);
+        case 2: return launch_token_fwd<DT, 2>(map, a, pl, sms, s);
+        default: return launch_token_fwd<DT, 1>(map, a, pl, sms, s);
+    }
+}
+
+// kNotApplicable when the table slices of all input columns do not fit one CTA
+inline int token_forward(const void* x, int x_dtype, const float* table, const float* bias, float* out,
+                         int64_t N, int64_t IN, int64_t OUT, const BinCfg& c, int sms, cudaStream_t s) {
+    FwdPlan pl;
+    if (!plan_token_forward(N, c.K, (int)IN, (int)OUT, sms, pl)) return kNotApplicable;
+    CUtensorMap map;
+    if (!make_table_map(&map, table, c.K, (int)IN, (int)OUT, pl.RS, pl.KB)) return kNotApplicable;
+    FwdArgs a;
+    a.x = x;
+    a.bias = bias;
+    a.out = out;
+    a.N = (int)N;
+    a.IN = (int)IN;
+    a.OUT = (int)OUT;
+    a.K = c.K;
+    a.JR = pl.JR;
+    a.RS = pl.RS;
+    a.xvec = (IN % 4 == 0) && ((uintptr_t)x % (x_dtype == kBF16 ? 8 : 16) == 0);
+    a.IG = pl.IG;
+    a.KB = pl.KB;
+    a.nbox = pl.nbox;
+    a.slice_bytes = pl.slice_bytes;
+    a.ntiles = 0;  // set per launch: tokens per CTA range
+    a.cfg = c;
+    return x_dtype == kBF16 ? launch_token_fwd_c<kBF16>(map, a, pl, sms, s)
+                            : launch_token_fwd_c<kF32>(map, a, pl, sms, s);
+}
+
+}  // namespace il

@@ -1,0 +1,389 @@
+// il_sorted.cuh -- backward of IndexedLinear by bin-sorted walks.
+//
+//   dx[n,i]  = sum_j go[n,j] * ((1-fr-s) T[lo,i,j] + (fr+s) T[hi,i,j])
+//   gt[k,i,:] = sum_{n: lo=k} x(1-fr) go[n,:] + sum_{n: hi=k} x fr go[n,:]
+//   gb[:]     = sum_n go[n,:]
+//
+// (s = x/bw where torch.clamp passes the gradient of fr, else 0) are the
+// gradients autograd produces for the reference's eager forward
+// (aiwn/layers/indexed_linear.py:173-182): the scatter-add into gt is the
+// backward of the gathers table[bk, ie] / table[hi, ie].
+//
+// A CTA owns one input column i and a range of tokens.  Per tile of up to
+// kSrtMaxTile tokens it
+//   1. bins every token (bit-exact, bw = 2^-e) and takes a rank inside its
+//      bin from a shared-memory counter,
+//   2. scans the bin counts into bin starts,
+//   3. writes (token, bin) and the four weights (x(1-fr), x fr, 1-fr-s,
+//      fr+s) of every token to its sorted position,
+//   4. cuts the sorted entries into equal slices, one per lane group (C
+//      lanes, one 16-byte chunk of a go row each).  A group walks its slice
+//      in bin order with
+//        - rows T[bin] and T[bin+1] of the column in registers (re-read from
+//          the column's table slice in shared memory when the bin changes),
+//        - two register accumulators, for gt rows bin and bin+1, added into
+//          gt with red.global.add.v4 only when the bin changes,
+//        - dx of each entry as a sum over the group's lanes,
+//      reading go rows from global memory (L2) kSrtDepth entries ahead.
+// Each gt row therefore receives one reduction per (lane group, tile) that
+// touches it instead of one per token: at 131072 tokens, 20 columns and
+// K=512 about 1 M vector reductions instead of 26 M.
+//
+// The order inside a bin follows shared-memory atomics, so the fp32 sums of
+// gt are not bitwise reproducible from run to run; dx is (each entry's dot
+// products do not depend on the order).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "il_common.cuh"
+#include "il_fast.cuh"
+#include "il_sm100.cuh"
+
+namespace il {
+
+constexpr int kSrtThreads = 1024;
+constexpr int kSrtPer = 8;                            // tokens per thread per tile
+constexpr int kSrtMaxTile = kSrtThreads * kSrtPer;    // 8192
+constexpr int kSrtTokBits = 14;                       // tile-local token bits of an entry
+constexpr uint32_t kSrtTokMask = (1u << kSrtTokBits) - 1u;
+constexpr int kSrtDepth = 3;                          // go rows in flight per lane group
+static_assert(kSrtMaxTile <= (1 << kSrtTokBits), "tile-local token index must fit the entry");
+
+struct SrtArgs {
+    const float* go;
+    const void* x;
+    const float* table;
+    void* gx;
+    float* gt;
+    float* gb;
+    int N, IN, OUT, K;
+    int TT;           // tokens per tile (multiple of 32, <= kSrtMaxTile)
+    int tok_per_cta;  // tokens of one CTA's range
+    int want_gx, want_gb;  // gt is always written (the kernel is chosen for it)
+    BinCfg cfg;
+};
+
+__device__ __forceinline__ void srt_flush(float* gt, int64_t row_stride, int row, int i, int OUT, int gl,
+                                          float4 v) {
+    red_global_add_v4(gt + ((int64_t)row * row_stride + i) * OUT + 4 * gl, v);
+}
+
+// Walk of one lane group over its sorted entries [e0, e1) of a tile.  The
+// trip count `steps` (a multiple of kSrtDepth) is the same for every lane of
+// the warp, since the dx sums use shuffles; steps past e1 read the weights of
+// the all-zero entry TT, and prefetches past the slice re-read its last entry
+// (always a valid address), so the common path has no branch except the one
+// taken when the bin changes.
+template <int DT, int C, bool GX>
+__device__ __forceinline__ void srt_walk(const SrtArgs& p, uint32_t slice_s, uint32_t ew_s, uint32_t en_s,
+                                         int t0, int e0, int e1, int steps, int gl, int i) {
+    const int OUT = p.OUT, IN = p.IN, K = p.K;
+    const float* gob = p.go + (int64_t)t0 * OUT + 4 * gl;
+    const int64_t gx0 = (int64_t)t0 * IN + i;
+    const int elast = max(e1 - 1, 0);
+    const uint32_t row_bytes = (uint32_t)OUT * 4;
+    const uint32_t tcol = slice_s + 16u * (uint32_t)gl;  // this lane's chunk of table row 0
+    uint32_t rn[kSrtDepth];
+    float4 rg[kSrtDepth];
+#pragma unroll
+    for (int d = 0; d < kSrtDepth; ++d) {
+        rn[d] = lds_u32(en_s + 4u * (uint32_t)min(e0 + d, elast));
+        rg[d] = __ldg(reinterpret_cast<const float4*>(gob + (rn[d] & kSrtTokMask) * OUT));
+    }
+    int cur = -1;
+    float4 tlo = make_float4(0.f, 0.f, 0.f, 0.f), thi = tlo, acl = tlo, ach = tlo;
+    for (int b = 0; b < steps; b += kSrtDepth) {
+#pragma unroll
+        for (int d = 0; d < kSrtDepth; ++d) {
+            const int e = e0 + b + d;
+            const bool valid = e < e1;
+            const uint32_t ent = rn[d];
+            const float4 g = rg[d];
+            rn[d] = lds_u32(en_s + 4u * (uint32_t)min(e + kSrtDepth, elast));
+            rg[d] = __ldg(reinterpret_cast<const float4*>(gob + (rn[d] & kSrtTokMask) * OUT));
+            const int bin = valid ? (int)(ent >> kSrtTokBits) : cur;
+            if (bin != cur) {
+                if (cur >= 0) {
+                    // row cur is complete; row cur+1 continues as the new low
+                    // row when the next bin is cur+1
+                    srt_flush(p.gt, IN, cur, i, OUT, gl, acl);
+                    if (bin == cur + 1) {
+                        acl = ach;
+                    } else {
+                        srt_flush(p.gt, IN, cur + 1, i, OUT, gl, ach);
+                        acl = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                    ach = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+                cur = bin;
+                tlo = lds_v4(tcol + (uint32_t)bin * row_bytes);
+                thi = lds_v4(tcol + (uint32_t)(bin + 1) * row_bytes);
+            }
+            const float4 w = lds_v4(ew_s + 16u * (uint32_t)(valid ? e : p.TT));
+            acl.x = fmaf(w.x, g.x, acl.x);
+            acl.y = fmaf(w.x, g.y, acl.y);
+            acl.z = fmaf(w.x, g.z, acl.z);
+            acl.w = fmaf(w.x, g.w, acl.w);
+            ach.x = fmaf(w.y, g.x, ach.x);
+            ach.y = fmaf(w.y, g.y, ach.y);
+            ach.z = fmaf(w.y, g.z, ach.z);
+            ach.w = fmaf(w.y, g.w, ach.w);
+            if constexpr (GX) {
+                const float dl = g.x * tlo.x + g.y * tlo.y + g.z * tlo.z + g.w * tlo.w;
+                const float dh = g.x * thi.x + g.y * thi.y + g.z * thi.z + g.w * thi.w;
+                float part = w.z * dl + w.w * dh;
+                // sum over the group's C lanes into its lane 0
+#pragma unroll
+                for (int off = 1; off < C; off <<= 1) {
+                    const float o = __shfl_down_sync(0xffffffffu, part, off);
+                    if (gl + off < C) part += o;
+                }
+                if (valid && gl == 0) store_gx<DT>(p.gx, gx0 + (int64_t)(ent & kSrtTokMask) * IN, part);
+            }
+        }
+    }
+    if (cur >= 0) {
+        // the top bin's hi row is row K-1 itself
+        if (cur == K - 1) {
+            acl.x += ach.x;
+            acl.y += ach.y;
+            acl.z += ach.z;
+            acl.w += ach.w;
+            srt_flush(p.gt, IN, cur, i, OUT, gl, acl);
+        } else {
+            srt_flush(p.gt, IN, cur, i, OUT, gl, acl);
+            srt_flush(p.gt, IN, cur + 1, i, OUT, gl, ach);
+        }
+    }
+}
+
+template <int DT, int C>
+__global__ void __launch_bounds__(kSrtThreads, 1) bwd_sorted_kernel(const SrtArgs p) {
+    static_assert(C >= 1 && C <= 32, "one go row per lane group of at most 32 lanes");
+    constexpr int GPW = 32 / C;                       // lane groups per warp
+    constexpr int NG = GPW * (kSrtThreads / 32);      // lane groups per CTA
+    extern __shared__ unsigned char smem[];
+    const int i = blockIdx.y;
+    const int K = p.K, OUT = p.OUT, IN = p.IN, TT = p.TT;
+    const int r0 = blockIdx.x * p.tok_per_cta;
+    const int r1 = min(p.N, r0 + p.tok_per_cta);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gw = lane / C, gl = lane - gw * C;      // group in warp, lane in group
+    const bool glive = gw < GPW;                      // lanes past the last full group idle
+    const int grp = warp * GPW + gw;
+
+    // shared memory (from a 128-byte aligned base):
+    //   slice [K+1][OUT] f32 | ew [TT+1] float4 (entry TT all zero) | en [TT] u32 | cnt [K+1] |
+    //   start [K+1] | tmp [32] | gbs [OUT]
+    const uint32_t base = (smem_addr(smem) + 127u) & ~127u;
+    float* slice = reinterpret_cast<float*>(smem + (base - smem_addr(smem)));
+    float4* ew = reinterpret_cast<float4*>(slice + (size_t)(K + 1) * OUT);
+    uint32_t* en = reinterpret_cast<uint32_t*>(ew + TT + 1);
+    uint32_t* cnt = en + TT;
+    uint32_t* start = cnt + (K + 1);
+    uint32_t* tmp = start + (K + 1);
+    float* gbs = reinterpret_cast<float*>(tmp + 32);
+
+    // the column's table slice T[:, i, :], plus row K = row K-1 (the
+    // reference's hi for the top bin), so that row bin+1 always exists
+    const uint32_t slice_s = base;
+    const uint32_t ew_s = slice_s + (uint32_t)((K + 1) * OUT * 4);
+    const uint32_t en_s = ew_s + 16u * (uint32_t)(TT + 1);
+    const uint32_t cnt_s = en_s + 4u * (uint32_t)TT;
+    for (int e = threadIdx.x; e < K * C; e += kSrtThreads) {
+        const int k = e / C, c4 = e - k * C;
+        const float4 v = __ldg(reinterpret_cast<const float4*>(p.table + ((int64_t)k * IN + i) * OUT) + c4);
+        sts_v4(slice_s + (uint32_t)((k * OUT + 4 * c4) * 4), v);
+        if (k == K - 1) sts_v4(slice_s + (uint32_t)((K * OUT + 4 * c4) * 4), v);
+    }
+    for (int e = threadIdx.x; e < K + 1; e += kSrtThreads) cnt[e] = 0;
+    for (int e = threadIdx.x; e < OUT; e += kSrtThreads) gbs[e] = 0.f;
+    if (threadIdx.x == 0) sts_v4(ew_s + 16u * (uint32_t)TT, make_float4(0.f, 0.f, 0.f, 0.f));
+    __syncthreads();
+
+    const int ntile = r1 > r0 ? (r1 - r0 + TT - 1) / TT : 0;
+    for (int t = 0; t < ntile; ++t) {
+        const int t0 = r0 + t * TT;
+        const int nt = min(TT, r1 - t0);
+        // 1. bins and ranks inside the bins (x values stay in registers)
+        float xr[kSrtPer];
+        uint32_t br[kSrtPer];
+#pragma unroll
+        for (int m = 0; m < kSrtPer; ++m) {
+            const int tl = threadIdx.x + m * kSrtThreads;
+            xr[m] = tl < nt ? load_x<DT>(p.x, (int64_t)(t0 + tl) * IN + i) : 0.0f;
+        }
+#pragma unroll
+        for (int m = 0; m < kSrtPer; ++m) {
+            const int tl = threadIdx.x + m * kSrtThreads;
+            br[m] = 0;
+            if (tl < nt) {
+                int lo;
+                float fr, frp;
+                bwd_bin<DT>(xr[m], p.cfg, lo, fr, frp);
+                br[m] = ((uint32_t)lo << 16) | atom_add_shared_u32(cnt_s + 4u * (uint32_t)lo, 1u);
+            }
+        }
+        __syncthreads();
+        // 2. bin starts
+        block_exclusive_scan<kSrtThreads>(cnt, start, K, tmp);
+        __syncthreads();
+        // 3. entries into bin order
+#pragma unroll
+        for (int m = 0; m < kSrtPer; ++m) {
+            const int tl = threadIdx.x + m * kSrtThreads;
+            if (tl < nt) {
+                const float xv = xr[m];
+                int lo;
+                float fr, frp;
+                bwd_bin<DT>(xv, p.cfg, lo, fr, frp);
+                const float omf = __fsub_rn(1.0f, fr);
+                const float sl = clamp_passes(frp) ? __fmul_rn(xv, p.cfg.inv) : 0.0f;
+                const uint32_t pos = start[lo] + (br[m] & 0xffffu);
+                sts_u32(en_s + 4u * pos, ((uint32_t)lo << kSrtTokBits) | (uint32_t)tl);
+                sts_v4(ew_s + 16u * pos, make_float4(omf == 0.0f ? 0.0f : __fmul_rn(xv, omf),
+                                                     fr == 0.0f ? 0.0f : __fmul_rn(xv, fr), omf - sl, fr + sl));
+            }
+        }
+        for (int e = threadIdx.x; e < K + 1; e += kSrtThreads) cnt[e] = 0;  // last read by the scan
+        __syncthreads();
+
+        // 4. walk: every group takes `per` consecutive entries
+        const int per = (nt + NG - 1) / NG;
+        const int e0 = glive ? min(nt, grp * per) : nt;
+        const int e1 = glive ? min(nt, e0 + per) : nt;
+        const int steps = (per + kSrtDepth - 1) / kSrtDepth * kSrtDepth;
+        if (p.want_gx) srt_walk<DT, C, true>(p, slice_s, ew_s, en_s, t0, e0, e1, steps, gl, i);
+        else srt_walk<DT, C, false>(p, slice_s, ew_s, en_s, t0, e0, e1, steps, gl, i);
+        __syncthreads();  // the next tile rewrites the entries
+    }
+    if (p.want_gb) {
+        // bias gradient: the IN CTAs of a token range split it into IN parts;
+        // thread t adds chunk t % C of every (1024/C)*C-th go row chunk
+        const int q = (r1 - r0 + IN - 1) / IN;
+        const int a0 = min(r1, r0 + i * q), a1 = min(r1, a0 + q);
+        constexpr int kStride = (kSrtThreads / C) * C;
+        float4 bsum = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (threadIdx.x < kStride) {
+            const float4* g4 = reinterpret_cast<const float4*>(p.go + (int64_t)a0 * OUT);
+            const int64_t n4 = (int64_t)(a1 - a0) * C;
+            for (int64_t e = threadIdx.x; e < n4; e += kStride) {
+                const float4 v = __ldg(g4 + e);
+                bsum.x += v.x;
+                bsum.y += v.y;
+                bsum.z += v.z;
+                bsum.w += v.w;
+            }
+            const int c = (int)threadIdx.x % C;
+            atomicAdd(gbs + 4 * c + 0, bsum.x);
+            atomicAdd(gbs + 4 * c + 1, bsum.y);
+            atomicAdd(gbs + 4 * c + 2, bsum.z);
+            atomicAdd(gbs + 4 * c + 3, bsum.w);
+        }
+        __syncthreads();
+        if (a1 > a0)
+            for (int e = threadIdx.x; e < OUT; e += kSrtThreads) atomicAdd(p.gb + e, gbs[e]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+struct SrtPlan {
+    int C = 0, TT = 0, R = 0, tok_per_cta = 0, smem = 0;
+};
+
+constexpr int kSrtChunks[] = {32, 20, 16, 10, 8, 5, 4, 2, 1};
+
+inline bool plan_sorted(int64_t N, int K, int IN, int OUT, int sms, SrtPlan& pl) {
+    if (OUT % 4 != 0 || OUT / 4 > 32 || K < 1 || K > 65535 || IN > 65535) return false;
+    const int C = OUT / 4;
+    bool inst = false;
+    for (int c : kSrtChunks) inst |= (c == C);
+    if (!inst) return false;
+    // bytes that do not scale with the tile: alignment, table slice, bin
+    // counters and starts, scan scratch, bias partials
+    const int64_t fixed = 128 + (int64_t)(K + 1) * OUT * 4 + 16 + (int64_t)(2 * K + 2) * 4 + 32 * 4 + OUT * 4;
+    const int64_t per_tok = 16 + 4;  // weights + packed (bin, token)
+    int64_t ttmax = (kSmemBudget - fixed) / per_tok;
+    ttmax = std::min<int64_t>(ttmax, kSrtMaxTile) / 32 * 32;
+    // a tile must give the rows some reuse: below 2 entries per bin the
+    // gather kernel's direct reductions are as good
+    if (ttmax < 512 || ttmax < 2 * (int64_t)K) return false;
+    int R = std::max(1, sms / IN);
+    R = (int)std::min<int64_t>(R, (N + 511) / 512);
+    R = std::max(R, 1);
+    const int64_t S = (N + R - 1) / R;
+    const int64_t ntile = (S + ttmax - 1) / ttmax;
+    const int64_t tt = std::min<int64_t>(ttmax, ((S + ntile - 1) / ntile + 31) / 32 * 32);
+    const int64_t per = ((S + tt - 1) / tt) * tt;  // tiles of one CTA tile its range exactly
+    R = (int)((N + per - 1) / per);
+    if (per > INT32_MAX / 2) return false;
+    pl = {C, (int)tt, R, (int)per, (int)(fixed + per_tok * tt)};
+    return true;
+}
+
+template <int DT, int C>
+inline int launch_sorted(const SrtArgs& a, const SrtPlan& pl, cudaStream_t s) {
+    auto kern = bwd_sorted_kernel<DT, C>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem) != cudaSuccess)
+        return 4;
+    kern<<<dim3((unsigned)pl.R, (unsigned)a.IN, 1), kSrtThreads, pl.smem, s>>>(a);
+    return 0;
+}
+
+template <int DT>
+inline int launch_sorted_c(const SrtArgs& a, const SrtPlan& pl, cudaStream_t s) {
+    switch (pl.C) {
+        case 32: return launch_sorted<DT, 32>(a, pl, s);
+        case 20: return launch_sorted<DT, 20>(a, pl, s);
+        case 16: return launch_sorted<DT, 16>(a, pl, s);
+        case 10: return launch_sorted<DT, 10>(a, pl, s);
+        case 8: return launch_sorted<DT, 8>(a, pl, s);
+        case 5: return launch_sorted<DT, 5>(a, pl, s);
+        case 4: return launch_sorted<DT, 4>(a, pl, s);
+        case 2: return launch_sorted<DT, 2>(a, pl, s);
+        default: return launch_sorted<DT, 1>(a, pl, s);
+    }
+}
+
+inline bool sorted_backward_ok(const float* go, const void* x, int x_dtype, const float* table, const void* gx,
+                               const float* gt, const float* gb, int64_t N, int64_t IN, int64_t OUT,
+                               int64_t K, const BinCfg& c) {
+    if (!c.pow2 || gt == nullptr) return false;  // bins written for bw = 2^-e; gt is what it is for
+    if (N > ((int64_t)1 << 30) || IN > 65535 || K > 65535) return false;
+    if (((uintptr_t)go | (uintptr_t)table | (uintptr_t)gt) & 15) return false;
+    if (x_dtype == kBF16 ? (((uintptr_t)x | (uintptr_t)gx) & 1) : (((uintptr_t)x | (uintptr_t)gx) & 3))
+        return false;
+    (void)gb;
+    return true;
+}
+
+// gt and gb must already be zero.  Returns kNotApplicable when the shape has
+// no plan (the caller then takes the gather kernel or the general kernels).
+inline int sorted_backward(const float* go, const void* x, int x_dtype, const float* table, void* gx, float* gt,
+                           float* gb, int64_t N, int64_t IN, int64_t OUT, const BinCfg& c, int sms,
+                           cudaStream_t s) {
+    SrtPlan pl;
+    if (!plan_sorted(N, c.K, (int)IN, (int)OUT, sms, pl)) return kNotApplicable;
+    SrtArgs a;
+    a.go = go;
+    a.x = x;
+    a.table = table;
+    a.gx = gx;
+    a.gt = gt;
+    a.gb = gb;
+    a.N = (int)N;
+    a.IN = (int)IN;
+    a.OUT = (int)OUT;
+    a.K = c.K;
+    a.TT = pl.TT;
+    a.tok_per_cta = pl.tok_per_cta;
+    a.want_gx = gx != nullptr;
+    a.want_gb = gb != nullptr;
+    a.cfg = c;
+    return x_dtype == kBF16 ? launch_sorted_c<kBF16>(a, pl, s) : launch_sorted_c<kF32>(a, pl, s);
+}
+
+}  // namespace il
