@@ -48,6 +48,9 @@ constexpr int kSrtMaxTile = kSrtThreads * kSrtPer;    // 8192
 constexpr int kSrtTokBits = 14;                       // tile-local token bits of an entry
 constexpr uint32_t kSrtTokMask = (1u << kSrtTokBits) - 1u;
 constexpr int kSrtDepth = 3;                          // go rows in flight per lane group
+constexpr int kSrtCtasPerSm = 1;                      // co-resident CTAs the plan sizes for
+// dynamic shared memory per CTA when kSrtCtasPerSm share an SM's 228 KB
+constexpr int kSrtSmemBudget = kSrtCtasPerSm == 1 ? kSmemBudget : (228 * 1024) / kSrtCtasPerSm - 1024 - 256;
 static_assert(kSrtMaxTile <= (1 << kSrtTokBits), "tile-local token index must fit the entry");
 
 struct SrtArgs {
@@ -159,7 +162,7 @@ __device__ __forceinline__ void srt_walk(const SrtArgs& p, uint32_t slice_s, uin
 }
 
 template <int DT, int C>
-__global__ void __launch_bounds__(kSrtThreads, 1) bwd_sorted_kernel(const SrtArgs p) {
+__global__ void __launch_bounds__(kSrtThreads, kSrtCtasPerSm) bwd_sorted_kernel(const SrtArgs p) {
     static_assert(C >= 1 && C <= 32, "one go row per lane group of at most 32 lanes");
     constexpr int GPW = 32 / C;                       // lane groups per warp
     constexpr int NG = GPW * (kSrtThreads / 32);      // lane groups per CTA
@@ -306,12 +309,12 @@ inline bool plan_sorted(int64_t N, int K, int IN, int OUT, int sms, SrtPlan& pl)
     // counters and starts, scan scratch, bias partials
     const int64_t fixed = 128 + (int64_t)(K + 1) * OUT * 4 + 16 + (int64_t)(2 * K + 2) * 4 + 32 * 4 + OUT * 4;
     const int64_t per_tok = 16 + 4;  // weights + packed (bin, token)
-    int64_t ttmax = (kSmemBudget - fixed) / per_tok;
+    int64_t ttmax = (kSrtSmemBudget - fixed) / per_tok;
     ttmax = std::min<int64_t>(ttmax, kSrtMaxTile) / 32 * 32;
     // a tile must give the rows some reuse: below 2 entries per bin the
     // gather kernel's direct reductions are as good
     if (ttmax < 512 || ttmax < 2 * (int64_t)K) return false;
-    int R = std::max(1, sms / IN);
+    int R = std::max(1, sms * kSrtCtasPerSm / IN);
     R = (int)std::min<int64_t>(R, (N + 511) / 512);
     R = std::max(R, 1);
     const int64_t S = (N + R - 1) / R;
