@@ -71,7 +71,8 @@ int check_common(const void* x, int x_dtype, int64_t N, int64_t IN, int64_t K, d
 // restrict il_forward / il_backward to the named family (shapes it cannot take
 // fall through to the general kernels).  Unset, or any other value, selects
 // automatically: forward with one token per lane when every input column's
-// table slice fits one CTA, else the cluster kernel; backward by the bin-sorted
+// table slice fits one CTA, else one token per lane with the table streamed
+// through shared memory (K <= 256), else the cluster kernel; backward by the bin-sorted
 // walk whenever the table gradient is wanted and the shape has a plan, else the
 // gather kernel.  The families compute the same results; the switches let the
 // tests cover each of them.
@@ -135,8 +136,19 @@ int il_forward(const void* x, int x_dtype, const float* table, const float* bias
     cudaStream_t s = (cudaStream_t)stream;
     const il::BinCfg c = make_cfg(bw, K);
     const KernelChoice path = kernel_choice("AIWN_IL_FORWARD", "token", "cluster");
-    if (path != kOnlyOther && il::fast_forward_ok(x, x_dtype, table, bias, out, N, IN, OUT, K, c)) {
+    if (path != kOnlyOther && il::fast_forward_args_ok(x, x_dtype, table, bias, out, N, IN, OUT, K, c)) {
         const int rc = il::token_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s);
+        if (rc != il::kNotApplicable) {
+            if (rc) {
+                cudaGetLastError();
+                return IL_ERR_LAUNCH;
+            }
+            return launch_status();
+        }
+    }
+    if (path != kOnlyOther && il::fast_forward_args_ok(x, x_dtype, table, bias, out, N, IN, OUT, K, c)) {
+        // tables too large to keep resident: stream column chunks through shared memory
+        const int rc = il::stream_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, s);
         if (rc != il::kNotApplicable) {
             if (rc) {
                 cudaGetLastError();

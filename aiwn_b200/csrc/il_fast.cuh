@@ -417,13 +417,15 @@ inline EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 3-D map of table [K][IN][OUT] fp32 with box {JR, 1, KB}
-inline bool make_table_map(CUtensorMap* m, const float* table, int K, int IN, int OUT, int JR, int KB) {
+// 3-D map of table [K][IN][OUT] fp32 with box {JR, COLS, KB} (shared-memory
+// layout of one box: [KB rows][COLS input columns][JR floats])
+inline bool make_table_map(CUtensorMap* m, const float* table, int K, int IN, int OUT, int JR, int KB,
+                           int COLS = 1) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[3] = {(cuuint64_t)OUT, (cuuint64_t)IN, (cuuint64_t)K};
     const cuuint64_t strides[2] = {(cuuint64_t)OUT * 4, (cuuint64_t)IN * OUT * 4};
-    const cuuint32_t box[3] = {(cuuint32_t)JR, 1u, (cuuint32_t)KB};
+    const cuuint32_t box[3] = {(cuuint32_t)JR, (cuuint32_t)COLS, (cuuint32_t)KB};
     const cuuint32_t estr[3] = {1u, 1u, 1u};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(table), dims, strides, box,
               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -474,14 +476,22 @@ inline bool plan_forward(int K, int IN, int OUT, FwdPlan& pl) {
     return false;
 }
 
-inline bool fast_forward_ok(const void* x, int x_dtype, const float* table, const float* bias,
-                            const float* out, int64_t N, int64_t IN, int64_t OUT, int64_t K,
-                            const BinCfg& c) {
+// argument conditions shared by the shape-specialised forwards
+inline bool fast_forward_args_ok(const void* x, int x_dtype, const float* table, const float* bias,
+                                 const float* out, int64_t N, int64_t IN, int64_t OUT, int64_t K,
+                                 const BinCfg& c) {
     if (!c.pow2) return false;  // the gather's bucketing is written for bw = 2^-e
     if (OUT % 4 != 0 || N > (int64_t)1 << 30 || IN > 65535 || K > 65535) return false;
     if (N * IN > ((int64_t)1 << 40)) return false;
     if (((uintptr_t)table | (uintptr_t)bias | (uintptr_t)out) & 15) return false;
     if (x_dtype == kBF16 ? ((uintptr_t)x & 1) : ((uintptr_t)x & 3)) return false;
+    return true;
+}
+
+inline bool fast_forward_ok(const void* x, int x_dtype, const float* table, const float* bias,
+                            const float* out, int64_t N, int64_t IN, int64_t OUT, int64_t K,
+                            const BinCfg& c) {
+    if (!fast_forward_args_ok(x, x_dtype, table, bias, out, N, IN, OUT, K, c)) return false;
     FwdPlan pl;
     return plan_forward((int)K, (int)IN, (int)OUT, pl);
 }

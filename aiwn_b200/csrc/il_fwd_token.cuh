@@ -230,4 +230,187 @@ inline int token_forward(const void* x, int x_dtype, const float* table, const f
                             : launch_token_fwd_c<kF32>(map, a, pl, sms, s);
 }
 
+
+// ---------------------------------------------------------------------------
+// streamed variant for tables too large to keep resident (e.g. 1024 x 1024
+// columns at K=64, 256 MB)
+// ---------------------------------------------------------------------------
+//
+// A CTA owns one tile of kStrThreads tokens (one per thread) and one j-range
+// of JR = 4*C output columns, and streams the table through shared memory in
+// chunks of CB input columns: one TMA box {RS floats, CB columns, K rows} per
+// chunk, two buffers, so that chunk c+1 lands while chunk c is used.  A box
+// lays rows out as [K][CB][RS]; row k of column s is (k*CB + s)*RS floats in,
+// and with RS/4 and CB both odd consecutive rows of a column start in
+// different bank groups.  hi = min(lo+1, K-1) is read from the box directly
+// (no extra row).  Each thread keeps its token's JR accumulators in registers
+// for the whole stream.
+constexpr int kStrThreads = 512;
+constexpr int kStrMaxCB = 15;  // input columns per chunk, at most (odd)
+
+struct StrArgs {
+    const void* x;
+    const float* bias;
+    float* out;
+    int N, IN, OUT, K;
+    int JR, RS;      // j-range width and shared-memory row stride (floats)
+    int CB;          // input columns per chunk (odd)
+    int nchunks;
+    int box_bytes;   // bytes of one chunk (K * CB * RS * 4)
+    int buf_stride;  // shared-memory bytes between the two buffers
+    BinCfg cfg;
+};
+
+template <int DT, int C>
+__global__ void __launch_bounds__(kStrThreads, 1)
+    fwd_stream_kernel(const __grid_constant__ CUtensorMap tmap, const StrArgs p) {
+    extern __shared__ unsigned char smem[];
+    const int IN = p.IN, K = p.K, CB = p.CB;
+    const int j0 = blockIdx.y * p.JR;
+    const int n = blockIdx.x * kStrThreads + (int)threadIdx.x;
+    const bool tok = n < p.N;
+    const uint32_t buf0 = (smem_addr(smem) + 127u) & ~127u;
+    const uint32_t bar0 = buf0 + 2u * (uint32_t)p.buf_stride;  // two mbarriers, 8 bytes each
+    const uint32_t row_bytes = (uint32_t)(CB * p.RS * 4);      // between rows k and k+1 of a column
+    const uint32_t col_bytes = (uint32_t)(p.RS * 4);
+
+    if (threadIdx.x == 0) {
+        prefetch_tensormap(&tmap);
+        mbar_init(bar0, 1);
+        mbar_init(bar0 + 8, 1);
+        fence_mbar_init();
+        for (int c = 0; c < 2 && c < p.nchunks; ++c) {
+            mbar_arrive_expect_tx(bar0 + 8u * c, (uint32_t)p.box_bytes);
+            tma_load_3d(buf0 + (uint32_t)(c * p.buf_stride), &tmap, bar0 + 8u * c, j0, c * CB, 0);
+        }
+    }
+    __syncthreads();
+
+    float4 acc[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int64_t xrow = (int64_t)(tok ? n : 0) * IN;
+
+    for (int ch = 0; ch < p.nchunks; ++ch) {
+        const int b = ch & 1;
+        const uint32_t buf = buf0 + (uint32_t)(b * p.buf_stride);
+        mbar_wait_bounded(bar0 + 8u * b, (uint32_t)((ch >> 1) & 1));
+        const int i0 = ch * CB;
+        const int ncol = min(CB, IN - i0);
+        float xs[kStrMaxCB];  // this chunk's x values of the token, loaded together
+#pragma unroll
+        for (int s = 0; s < kStrMaxCB; ++s) xs[s] = (tok && s < ncol) ? load_x<DT>(p.x, xrow + i0 + s) : 0.0f;
+#pragma unroll
+        for (int s = 0; s < kStrMaxCB; ++s) {
+            if (s >= ncol) break;
+            const float xv = xs[s];
+            int lo;
+            float wa, wc;
+            gather_weights<DT>(xv, p.cfg, lo, wa, wc);
+            const uint32_t rlo = buf + (uint32_t)lo * row_bytes + (uint32_t)s * col_bytes;
+            const uint32_t rhi = rlo + (lo < K - 1 ? row_bytes : 0u);
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+                const float4 tl = lds_v4(rlo + c * 16);
+                const float4 th = lds_v4(rhi + c * 16);
+                acc[c].x = fmaf(wa, tl.x, acc[c].x);
+                acc[c].y = fmaf(wa, tl.y, acc[c].y);
+                acc[c].z = fmaf(wa, tl.z, acc[c].z);
+                acc[c].w = fmaf(wa, tl.w, acc[c].w);
+                acc[c].x = fmaf(wc, th.x, acc[c].x);
+                acc[c].y = fmaf(wc, th.y, acc[c].y);
+                acc[c].z = fmaf(wc, th.z, acc[c].z);
+                acc[c].w = fmaf(wc, th.w, acc[c].w);
+            }
+        }
+        __syncthreads();  // every thread is done with this buffer
+        if (threadIdx.x == 0 && ch + 2 < p.nchunks) {
+            fence_proxy_async_smem();  // generic reads of the buffer before the async-proxy refill
+            mbar_arrive_expect_tx(bar0 + 8u * b, (uint32_t)p.box_bytes);
+            tma_load_3d(buf, &tmap, bar0 + 8u * b, j0, (ch + 2) * CB, 0);
+        }
+    }
+    if (tok) {
+        float4* o = reinterpret_cast<float4*>(p.out + (int64_t)n * p.OUT + j0);
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + j0) + c);
+            o[c] = make_float4(acc[c].x + bb.x, acc[c].y + bb.y, acc[c].z + bb.z, acc[c].w + bb.w);
+        }
+    }
+}
+
+constexpr int kStrChunks[] = {8, 4, 2, 1};
+
+struct StrPlan {
+    int C = 0, JR = 0, RS = 0, CB = 0, nchunks = 0, box_bytes = 0, buf_stride = 0, smem = 0;
+};
+
+// widest j-range (C <= 8) whose two chunk buffers of at least 3 columns fit;
+// the TMA box needs K <= 256 rows and CB <= 256 columns
+inline bool plan_stream_forward(int K, int IN, int OUT, StrPlan& pl) {
+    if (OUT % 4 != 0 || K > 256 || K < 2) return false;
+    const int chunks = OUT / 4;
+    for (int C : kStrChunks) {
+        if (chunks % C != 0) continue;
+        const int JR = 4 * C;
+        const int RS = (C % 2 == 0) ? JR + 4 : JR;  // RS/4 odd
+        const int col = K * RS * 4;                 // bytes of one column's rows
+        int CB = (kSmemBudget - 128 - 32) / 2 / col;
+        CB = std::min(CB, std::min(kStrMaxCB, IN));
+        if (CB % 2 == 0) --CB;  // odd: rows of a column spread over the bank groups
+        if (CB < 1) continue;
+        const int box = K * CB * RS * 4;
+        const int stride = round_up(box, 128);
+        pl = {C, JR, RS, CB, ceil_div(IN, CB), box, stride, 2 * stride + 128 + 32};
+        return true;
+    }
+    return false;
+}
+
+template <int DT, int C>
+inline int launch_stream_fwd(const CUtensorMap& map, const StrArgs& a, const StrPlan& pl, cudaStream_t s) {
+    auto kern = fwd_stream_kernel<DT, C>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem) != cudaSuccess)
+        return 4;
+    kern<<<dim3((unsigned)ceil_div(a.N, kStrThreads), (unsigned)(a.OUT / pl.JR), 1), kStrThreads, pl.smem, s>>>(map,
+                                                                                                             a);
+    return 0;
+}
+
+template <int DT>
+inline int launch_stream_fwd_c(const CUtensorMap& map, const StrArgs& a, const StrPlan& pl, cudaStream_t s) {
+    switch (pl.C) {
+        case 8: return launch_stream_fwd<DT, 8>(map, a, pl, s);
+        case 4: return launch_stream_fwd<DT, 4>(map, a, pl, s);
+        case 2: return launch_stream_fwd<DT, 2>(map, a, pl, s);
+        default: return launch_stream_fwd<DT, 1>(map, a, pl, s);
+    }
+}
+
+// kNotApplicable when the shape has no streaming plan
+inline int stream_forward(const void* x, int x_dtype, const float* table, const float* bias, float* out,
+                          int64_t N, int64_t IN, int64_t OUT, const BinCfg& c, cudaStream_t s) {
+    StrPlan pl;
+    if (!plan_stream_forward(c.K, (int)IN, (int)OUT, pl)) return kNotApplicable;
+    CUtensorMap map;
+    if (!make_table_map(&map, table, c.K, (int)IN, (int)OUT, pl.RS, c.K, pl.CB)) return kNotApplicable;
+    StrArgs a;
+    a.x = x;
+    a.bias = bias;
+    a.out = out;
+    a.N = (int)N;
+    a.IN = (int)IN;
+    a.OUT = (int)OUT;
+    a.K = c.K;
+    a.JR = pl.JR;
+    a.RS = pl.RS;
+    a.CB = pl.CB;
+    a.nchunks = pl.nchunks;
+    a.box_bytes = pl.box_bytes;
+    a.buf_stride = pl.buf_stride;
+    a.cfg = c;
+    return x_dtype == kBF16 ? launch_stream_fwd_c<kBF16>(map, a, pl, s) : launch_stream_fwd_c<kF32>(map, a, pl, s);
+}
+
 }  // namespace il

@@ -64,12 +64,14 @@ struct SrtArgs {
     int TT;           // tokens per tile (multiple of 32, <= kSrtMaxTile)
     int tok_per_cta;  // tokens of one CTA's range
     int want_gx, want_gb;  // gt is always written (the kernel is chosen for it)
+    int gx_atomic;         // several j-ranges: dx partial sums are added (gx zeroed, fp32)
     BinCfg cfg;
 };
 
-__device__ __forceinline__ void srt_flush(float* gt, int64_t row_stride, int row, int i, int OUT, int gl,
-                                          float4 v) {
-    red_global_add_v4(gt + ((int64_t)row * row_stride + i) * OUT + 4 * gl, v);
+// add a finished gradient row chunk: element offset row * IN*OUT + lane_off
+// (lane_off = i*OUT + j-range start + 4*lane; the plan keeps K*IN*OUT < 2^31)
+__device__ __forceinline__ void srt_flush(float* gt, int row, int rs, int lane_off, float4 v) {
+    red_global_add_v4(gt + (uint32_t)(row * rs + lane_off), v);
 }
 
 // Walk of one lane group over its sorted entries [e0, e1) of a tile.  The
@@ -78,14 +80,16 @@ __device__ __forceinline__ void srt_flush(float* gt, int64_t row_stride, int row
 // the all-zero entry TT, and prefetches past the slice re-read its last entry
 // (always a valid address), so the common path has no branch except the one
 // taken when the bin changes.
-template <int DT, int C, bool GX>
+template <int DT, int C, bool GX, bool GXA>
 __device__ __forceinline__ void srt_walk(const SrtArgs& p, uint32_t slice_s, uint32_t ew_s, uint32_t en_s,
                                          int t0, int e0, int e1, int steps, int gl, int i) {
     const int OUT = p.OUT, IN = p.IN, K = p.K;
-    const float* gob = p.go + (int64_t)t0 * OUT + 4 * gl;
+    const float* gob = p.go + (int64_t)t0 * OUT + blockIdx.z * 4 * C + 4 * gl;  // j-range blockIdx.z
     const int64_t gx0 = (int64_t)t0 * IN + i;
     const int elast = max(e1 - 1, 0);
-    const uint32_t row_bytes = (uint32_t)OUT * 4;
+    const uint32_t row_bytes = (uint32_t)C * 16;         // slice rows hold the j-range
+    const int rs = IN * OUT;                             // gt row stride (elements)
+    const int lane_off = i * OUT + (int)blockIdx.z * 4 * C + 4 * gl;
     const uint32_t tcol = slice_s + 16u * (uint32_t)gl;  // this lane's chunk of table row 0
     uint32_t rn[kSrtDepth];
     float4 rg[kSrtDepth];
@@ -110,11 +114,11 @@ __device__ __forceinline__ void srt_walk(const SrtArgs& p, uint32_t slice_s, uin
                 if (cur >= 0) {
                     // row cur is complete; row cur+1 continues as the new low
                     // row when the next bin is cur+1
-                    srt_flush(p.gt, IN, cur, i, OUT, gl, acl);
+                    srt_flush(p.gt, cur, rs, lane_off, acl);
                     if (bin == cur + 1) {
                         acl = ach;
                     } else {
-                        srt_flush(p.gt, IN, cur + 1, i, OUT, gl, ach);
+                        srt_flush(p.gt, cur + 1, rs, lane_off, ach);
                         acl = make_float4(0.f, 0.f, 0.f, 0.f);
                     }
                     ach = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -142,7 +146,11 @@ __device__ __forceinline__ void srt_walk(const SrtArgs& p, uint32_t slice_s, uin
                     const float o = __shfl_down_sync(0xffffffffu, part, off);
                     if (gl + off < C) part += o;
                 }
-                if (valid && gl == 0) store_gx<DT>(p.gx, gx0 + (int64_t)(ent & kSrtTokMask) * IN, part);
+                if (valid && gl == 0) {
+                    const int64_t at = gx0 + (int64_t)(ent & kSrtTokMask) * IN;
+                    if constexpr (GXA) atomicAdd(reinterpret_cast<float*>(p.gx) + at, part);
+                    else store_gx<DT>(p.gx, at, part);
+                }
             }
         }
     }
@@ -153,10 +161,10 @@ __device__ __forceinline__ void srt_walk(const SrtArgs& p, uint32_t slice_s, uin
             acl.y += ach.y;
             acl.z += ach.z;
             acl.w += ach.w;
-            srt_flush(p.gt, IN, cur, i, OUT, gl, acl);
+            srt_flush(p.gt, cur, rs, lane_off, acl);
         } else {
-            srt_flush(p.gt, IN, cur, i, OUT, gl, acl);
-            srt_flush(p.gt, IN, cur + 1, i, OUT, gl, ach);
+            srt_flush(p.gt, cur, rs, lane_off, acl);
+            srt_flush(p.gt, cur + 1, rs, lane_off, ach);
         }
     }
 }
@@ -177,11 +185,11 @@ __global__ void __launch_bounds__(kSrtThreads, kSrtCtasPerSm) bwd_sorted_kernel(
     const int grp = warp * GPW + gw;
 
     // shared memory (from a 128-byte aligned base):
-    //   slice [K+1][OUT] f32 | ew [TT+1] float4 (entry TT all zero) | en [TT] u32 | cnt [K+1] |
-    //   start [K+1] | tmp [32] | gbs [OUT]
+    //   slice [K+1][4C] f32 (the j-range of T[:, i, :]) | ew [TT+1] float4 (entry TT all zero) |
+    //   en [TT] u32 | cnt [K+1] | start [K+1] | tmp [32] | gbs [4C]
     const uint32_t base = (smem_addr(smem) + 127u) & ~127u;
     float* slice = reinterpret_cast<float*>(smem + (base - smem_addr(smem)));
-    float4* ew = reinterpret_cast<float4*>(slice + (size_t)(K + 1) * OUT);
+    float4* ew = reinterpret_cast<float4*>(slice + (size_t)(K + 1) * 4 * C);
     uint32_t* en = reinterpret_cast<uint32_t*>(ew + TT + 1);
     uint32_t* cnt = en + TT;
     uint32_t* start = cnt + (K + 1);
@@ -191,17 +199,18 @@ __global__ void __launch_bounds__(kSrtThreads, kSrtCtasPerSm) bwd_sorted_kernel(
     // the column's table slice T[:, i, :], plus row K = row K-1 (the
     // reference's hi for the top bin), so that row bin+1 always exists
     const uint32_t slice_s = base;
-    const uint32_t ew_s = slice_s + (uint32_t)((K + 1) * OUT * 4);
+    const uint32_t ew_s = slice_s + (uint32_t)((K + 1) * C * 16);
+    const int j0 = blockIdx.z * 4 * C;
     const uint32_t en_s = ew_s + 16u * (uint32_t)(TT + 1);
     const uint32_t cnt_s = en_s + 4u * (uint32_t)TT;
     for (int e = threadIdx.x; e < K * C; e += kSrtThreads) {
         const int k = e / C, c4 = e - k * C;
-        const float4 v = __ldg(reinterpret_cast<const float4*>(p.table + ((int64_t)k * IN + i) * OUT) + c4);
-        sts_v4(slice_s + (uint32_t)((k * OUT + 4 * c4) * 4), v);
-        if (k == K - 1) sts_v4(slice_s + (uint32_t)((K * OUT + 4 * c4) * 4), v);
+        const float4 v = __ldg(reinterpret_cast<const float4*>(p.table + ((int64_t)k * IN + i) * OUT + j0) + c4);
+        sts_v4(slice_s + (uint32_t)((k * C + c4) * 16), v);
+        if (k == K - 1) sts_v4(slice_s + (uint32_t)((K * C + c4) * 16), v);
     }
     for (int e = threadIdx.x; e < K + 1; e += kSrtThreads) cnt[e] = 0;
-    for (int e = threadIdx.x; e < OUT; e += kSrtThreads) gbs[e] = 0.f;
+    for (int e = threadIdx.x; e < 4 * C; e += kSrtThreads) gbs[e] = 0.f;
     if (threadIdx.x == 0) sts_v4(ew_s + 16u * (uint32_t)TT, make_float4(0.f, 0.f, 0.f, 0.f));
     __syncthreads();
 
@@ -257,28 +266,35 @@ __global__ void __launch_bounds__(kSrtThreads, kSrtCtasPerSm) bwd_sorted_kernel(
         const int e0 = glive ? min(nt, grp * per) : nt;
         const int e1 = glive ? min(nt, e0 + per) : nt;
         const int steps = (per + kSrtDepth - 1) / kSrtDepth * kSrtDepth;
-        if (p.want_gx) srt_walk<DT, C, true>(p, slice_s, ew_s, en_s, t0, e0, e1, steps, gl, i);
-        else srt_walk<DT, C, false>(p, slice_s, ew_s, en_s, t0, e0, e1, steps, gl, i);
+        if (p.want_gx && p.gx_atomic) {
+            // only the 128-column j-ranges of OUT > 128 split dx (fp32 x)
+            if constexpr (DT == kF32 && C == 32)
+                srt_walk<DT, C, true, true>(p, slice_s, ew_s, en_s, t0, e0, e1, steps, gl, i);
+        } else if (p.want_gx) {
+            srt_walk<DT, C, true, false>(p, slice_s, ew_s, en_s, t0, e0, e1, steps, gl, i);
+        } else {
+            srt_walk<DT, C, false, false>(p, slice_s, ew_s, en_s, t0, e0, e1, steps, gl, i);
+        }
         __syncthreads();  // the next tile rewrites the entries
     }
     if (p.want_gb) {
-        // bias gradient: the IN CTAs of a token range split it into IN parts;
-        // thread t adds chunk t % C of every (1024/C)*C-th go row chunk
+        // bias gradient of the j-range: the IN CTAs of a token range split it
+        // into IN parts; thread t adds chunk t % C of every (1024/C)-th row
         const int q = (r1 - r0 + IN - 1) / IN;
         const int a0 = min(r1, r0 + i * q), a1 = min(r1, a0 + q);
         constexpr int kStride = (kSrtThreads / C) * C;
         float4 bsum = make_float4(0.f, 0.f, 0.f, 0.f);
         if (threadIdx.x < kStride) {
-            const float4* g4 = reinterpret_cast<const float4*>(p.go + (int64_t)a0 * OUT);
+            const int c = (int)threadIdx.x % C;
+            const float* gj = p.go + (int64_t)a0 * OUT + j0 + 4 * c;
             const int64_t n4 = (int64_t)(a1 - a0) * C;
             for (int64_t e = threadIdx.x; e < n4; e += kStride) {
-                const float4 v = __ldg(g4 + e);
+                const float4 v = __ldg(reinterpret_cast<const float4*>(gj + (e / C) * OUT));
                 bsum.x += v.x;
                 bsum.y += v.y;
                 bsum.z += v.z;
                 bsum.w += v.w;
             }
-            const int c = (int)threadIdx.x % C;
             atomicAdd(gbs + 4 * c + 0, bsum.x);
             atomicAdd(gbs + 4 * c + 1, bsum.y);
             atomicAdd(gbs + 4 * c + 2, bsum.z);
@@ -286,7 +302,7 @@ __global__ void __launch_bounds__(kSrtThreads, kSrtCtasPerSm) bwd_sorted_kernel(
         }
         __syncthreads();
         if (a1 > a0)
-            for (int e = threadIdx.x; e < OUT; e += kSrtThreads) atomicAdd(p.gb + e, gbs[e]);
+            for (int e = threadIdx.x; e < 4 * C; e += kSrtThreads) atomicAdd(p.gb + j0 + e, gbs[e]);
     }
 }
 
@@ -294,27 +310,35 @@ __global__ void __launch_bounds__(kSrtThreads, kSrtCtasPerSm) bwd_sorted_kernel(
 // host side
 // ---------------------------------------------------------------------------
 struct SrtPlan {
-    int C = 0, TT = 0, R = 0, tok_per_cta = 0, smem = 0;
+    int C = 0, TT = 0, R = 0, tok_per_cta = 0, smem = 0, jranges = 1;
 };
 
 constexpr int kSrtChunks[] = {32, 20, 16, 10, 8, 5, 4, 2, 1};
 
+// j-ranges of 4*C output columns: one range when OUT/4 is an instantiated C,
+// else ranges of 128 columns (C = 32) when OUT is a multiple of 128
 inline bool plan_sorted(int64_t N, int K, int IN, int OUT, int sms, SrtPlan& pl) {
-    if (OUT % 4 != 0 || OUT / 4 > 32 || K < 1 || K > 65535 || IN > 65535) return false;
-    const int C = OUT / 4;
+    if (OUT % 4 != 0 || K < 1 || K > 65535 || IN > 65535) return false;
+    if ((int64_t)K * IN * OUT >= ((int64_t)1 << 31)) return false;  // 32-bit gt offsets
+    int C = OUT / 4, jranges = 1;
+    if (C > 32) {
+        if (OUT % 128 != 0) return false;
+        C = 32;
+        jranges = OUT / 128;
+    }
     bool inst = false;
     for (int c : kSrtChunks) inst |= (c == C);
     if (!inst) return false;
-    // bytes that do not scale with the tile: alignment, table slice, bin
-    // counters and starts, scan scratch, bias partials
-    const int64_t fixed = 128 + (int64_t)(K + 1) * OUT * 4 + 16 + (int64_t)(2 * K + 2) * 4 + 32 * 4 + OUT * 4;
+    // bytes that do not scale with the tile: alignment, table slice, zero
+    // entry, bin counters and starts, scan scratch, bias partials
+    const int64_t fixed = 128 + (int64_t)(K + 1) * C * 16 + 16 + (int64_t)(2 * K + 2) * 4 + 32 * 4 + C * 16;
     const int64_t per_tok = 16 + 4;  // weights + packed (bin, token)
     int64_t ttmax = (kSrtSmemBudget - fixed) / per_tok;
     ttmax = std::min<int64_t>(ttmax, kSrtMaxTile) / 32 * 32;
     // a tile must give the rows some reuse: below 2 entries per bin the
     // gather kernel's direct reductions are as good
     if (ttmax < 512 || ttmax < 2 * (int64_t)K) return false;
-    int R = std::max(1, sms * kSrtCtasPerSm / IN);
+    int R = std::max(1, sms * kSrtCtasPerSm / (IN * jranges));
     R = (int)std::min<int64_t>(R, (N + 511) / 512);
     R = std::max(R, 1);
     const int64_t S = (N + R - 1) / R;
@@ -323,7 +347,7 @@ inline bool plan_sorted(int64_t N, int K, int IN, int OUT, int sms, SrtPlan& pl)
     const int64_t per = ((S + tt - 1) / tt) * tt;  // tiles of one CTA tile its range exactly
     R = (int)((N + per - 1) / per);
     if (per > INT32_MAX / 2) return false;
-    pl = {C, (int)tt, R, (int)per, (int)(fixed + per_tok * tt)};
+    pl = {C, (int)tt, R, (int)per, (int)(fixed + per_tok * tt), jranges};
     return true;
 }
 
@@ -332,7 +356,7 @@ inline int launch_sorted(const SrtArgs& a, const SrtPlan& pl, cudaStream_t s) {
     auto kern = bwd_sorted_kernel<DT, C>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem) != cudaSuccess)
         return 4;
-    kern<<<dim3((unsigned)pl.R, (unsigned)a.IN, 1), kSrtThreads, pl.smem, s>>>(a);
+    kern<<<dim3((unsigned)pl.R, (unsigned)a.IN, (unsigned)pl.jranges), kSrtThreads, pl.smem, s>>>(a);
     return 0;
 }
 
@@ -370,6 +394,12 @@ inline int sorted_backward(const float* go, const void* x, int x_dtype, const fl
                            cudaStream_t s) {
     SrtPlan pl;
     if (!plan_sorted(N, c.K, (int)IN, (int)OUT, sms, pl)) return kNotApplicable;
+    // with several j-ranges each adds its part of dx: fp32 gx only, zeroed first
+    const bool gx_atomic = pl.jranges > 1 && gx != nullptr;
+    if (gx_atomic) {
+        if (x_dtype != kF32) return kNotApplicable;
+        if (cudaMemsetAsync(gx, 0, (size_t)(N * IN) * sizeof(float), s) != cudaSuccess) return 4;
+    }
     SrtArgs a;
     a.go = go;
     a.x = x;
@@ -385,6 +415,7 @@ inline int sorted_backward(const float* go, const void* x, int x_dtype, const fl
     a.tok_per_cta = pl.tok_per_cta;
     a.want_gx = gx != nullptr;
     a.want_gb = gb != nullptr;
+    a.gx_atomic = gx_atomic ? 1 : 0;
     a.cfg = c;
     return x_dtype == kBF16 ? launch_sorted_c<kBF16>(a, pl, s) : launch_sorted_c<kF32>(a, pl, s);
 }

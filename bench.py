@@ -45,6 +45,9 @@ CONFIGS = {
                   d=512, K=512, B=32, seq=4096, IN=20, OUT=80, xdist="uniform", dtype="f32"),
     "c4": dict(desc="IndexedLinear(1024, 1024, K=64), 16384 tokens per GPU, x=clamp(N(0,0.5)) fp32",
                d=1024, K=64, B=2, seq=8192, IN=1024, OUT=1024, xdist="clamp_normal", dtype="f32"),
+    "c5": dict(desc="IndexedGPT projection shape IndexedLinear(16, 16, K=128), batch 64 x ctx 256 "
+                    "(16384 tokens), x~U(-1,1) fp32", d=256, K=128, B=64, seq=256, IN=16, OUT=16,
+               xdist="uniform", dtype="f32"),
 }
 
 
@@ -307,6 +310,16 @@ def run_ours(args, cfg, world, rank, local):
 
     ms_train = time_calls(train_step, reps)
 
+    # the same step without the gradient all-reduce (multi-GPU runs): the
+    # difference is the exchange step's cost
+    ms_noar = None
+    if world > 1:
+        def step_local(k):
+            i = k % n_sets
+            _lib.forward(xs[i], table, bias, outs[i], bw)
+            _lib.backward(gos[i], xs[i], table, gxs[i], gt, gb, bw, ws if ws_n else None)
+        ms_noar = time_calls(step_local, reps)
+
     # end to end through the public module API, host buffers, copies inside
     m = TokenParallelIndexedLinear(IN, OUT, K, layer=IndexedLinear(IN, OUT, K)).to(dev)
     with torch.no_grad():
@@ -357,6 +370,8 @@ def run_ours(args, cfg, world, rank, local):
         "fwd_bwd_tokens_per_s": world * N / (ms_step * 1e-3),
         "train_step_tokens_per_s": world * N / (ms_train * 1e-3),
         "ms": {"fwd": ms_fwd, "bwd": ms_bwd, "fwd_bwd": ms_step, "train_step_adam": ms_train},
+        **({"fwd_bwd_without_allreduce": {"tokens_per_s": world * N / (ms_noar * 1e-3), "ms": ms_noar}}
+           if ms_noar is not None else {}),
         "hbm_roofline_frac": {
             "fwd": b_fwd / (ms_fwd * 1e-3) / 1e9 / hbm,
             "fwd_bwd": (b_fwd + b_bwd) / (ms_step * 1e-3) / 1e9 / hbm,
