@@ -54,6 +54,10 @@ def load():
         lib.il_bins.restype = ci
         lib.il_adam_step.argtypes = [vp, vp, vp, vp, i64, f64, f64, f64, f64, i64, vp]
         lib.il_adam_step.restype = ci
+        lib.il_cdf_forward.argtypes = [vp, vp, vp, f64, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, f64, vp]
+        lib.il_cdf_forward.restype = ci
+        lib.il_cdf_backward.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+        lib.il_cdf_backward.restype = ci
         lib.il_kernel_launches.argtypes = []
         lib.il_kernel_launches.restype = i64
         lib.il_check_device_status.argtypes = [vp]
@@ -149,6 +153,32 @@ def backward(go, x, table, gx, gt, gb, bw: float, workspace=None):
         _check(lib.il_backward(_p(go), _p(x), x_dtype_code(x), _p(table), _p(gx), _p(gt), _p(gb),
                                N, IN, OUT, K, float(bw), _p(workspace), ws_bytes,
                                _stream(x.device)), "il_backward")
+
+
+def cdf_forward(x, gamma, beta, eps: float, table, bias, xn, mean, rstd, out, bw: float):
+    """IndexedLinearV2 forward: xn <- GaussianCDFNorm(x), out <- IndexedLinear(xn);
+    also the per-token LayerNorm mean and rstd.  fp32 x [N, IN]."""
+    _need_cuda(x, gamma, beta, table, bias, xn, mean, rstd, out)
+    if x.dtype != torch.float32:
+        raise ILError("il_cdf_forward takes fp32 x")
+    N, IN = x.shape
+    K, _, OUT = table.shape
+    lib = load()
+    with _on_device(x.device):
+        _check(lib.il_cdf_forward(_p(x), _p(gamma), _p(beta), float(eps), _p(table), _p(bias), _p(xn), _p(mean),
+                                  _p(rstd), _p(out), N, IN, OUT, K, float(bw), _stream(x.device)),
+               "il_cdf_forward")
+    return out
+
+
+def cdf_backward(gxn, x, gamma, beta, mean, rstd, dx, dgamma, dbeta):
+    """dx / dgamma / dbeta (any may be None) <- backward of the GaussianCDFNorm prologue."""
+    _need_cuda(gxn, x, gamma, beta, mean, rstd, dx, dgamma, dbeta)
+    N, IN = x.shape
+    lib = load()
+    with _on_device(x.device):
+        _check(lib.il_cdf_backward(_p(gxn), _p(x), _p(gamma), _p(beta), _p(mean), _p(rstd), _p(dx), _p(dgamma),
+                                   _p(dbeta), N, IN, _stream(x.device)), "il_cdf_backward")
 
 
 def bins(x, K: int, bw: float):

@@ -9,6 +9,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 
@@ -18,6 +19,7 @@
 #include "il_fast.cuh"
 #include "il_sorted.cuh"
 #include "il_fwd_token.cuh"
+#include "il_cdf.cuh"
 
 namespace {
 
@@ -102,6 +104,49 @@ inline unsigned grid_for(int64_t work, int threads, int num_sms) {
     return (unsigned)(blocks < 1 ? 1 : blocks);
 }
 
+// kernel selection of the forward (arguments already checked)
+int forward_dispatch(const void* x, int x_dtype, const float* table, const float* bias, float* out, int64_t N,
+                     int64_t IN, int64_t OUT, const il::BinCfg& c, int sms, cudaStream_t s) {
+    const KernelChoice path = kernel_choice("AIWN_IL_FORWARD", "token", "cluster");
+    if (path != kOnlyOther && il::fast_forward_args_ok(x, x_dtype, table, bias, out, N, IN, OUT, c.K, c)) {
+        const int rc = il::token_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s);
+        if (rc != il::kNotApplicable) {
+            if (rc) {
+                cudaGetLastError();
+                return IL_ERR_LAUNCH;
+            }
+            return launch_status();
+        }
+    }
+    if (path != kOnlyOther && il::fast_forward_args_ok(x, x_dtype, table, bias, out, N, IN, OUT, c.K, c)) {
+        // tables too large to keep resident: stream column chunks through shared memory
+        const int rc = il::stream_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, s);
+        if (rc != il::kNotApplicable) {
+            if (rc) {
+                cudaGetLastError();
+                return IL_ERR_LAUNCH;
+            }
+            return launch_status();
+        }
+    }
+    if (path != kOnlyPreferred && il::fast_forward_ok(x, x_dtype, table, bias, out, N, IN, OUT, c.K, c)) {
+        const int rc = il::fast_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s);
+        if (rc != il::kNotApplicable) {
+            if (rc) {
+                cudaGetLastError();
+                return IL_ERR_LAUNCH;
+            }
+            return launch_status();
+        }
+    }
+    const unsigned g = grid_for(N * OUT, 256, sms);
+    if (x_dtype == IL_BF16)
+        il::fwd_simple_kernel<il::kBF16><<<g, 256, 0, s>>>(x, table, bias, out, N, IN, OUT, c);
+    else
+        il::fwd_simple_kernel<il::kF32><<<g, 256, 0, s>>>(x, table, bias, out, N, IN, OUT, c);
+    return launch_status();
+}
+
 }  // namespace
 
 extern "C" {
@@ -135,9 +180,27 @@ int il_forward(const void* x, int x_dtype, const float* table, const float* bias
     if ((st = check_device(&sms))) return st;
     cudaStream_t s = (cudaStream_t)stream;
     const il::BinCfg c = make_cfg(bw, K);
+    return forward_dispatch(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s);
+}
+
+int il_cdf_forward(const float* x, const float* gamma, const float* beta, double eps, const float* table,
+                   const float* bias, float* xn, float* mean, float* rstd, float* out, int64_t N, int64_t IN,
+                   int64_t OUT, int64_t K, double bw, void* stream) {
+    int st = check_common(x, IL_F32, N, IN, K, bw);
+    if (st) return st;
+    if (OUT < 1) return IL_ERR_SHAPE;
+    if (!(eps >= 0.0)) return IL_ERR_VALUE;
+    if (N == 0) return IL_OK;
+    if (!gamma || !beta || !table || !bias || !xn || !mean || !rstd || !out) return IL_ERR_NULL;
+    if (N > INT32_MAX) return IL_ERR_SHAPE;
+    int sms = 0;
+    if ((st = check_device(&sms))) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    const il::BinCfg c = make_cfg(bw, K);
+    const il::CdfArgs q{gamma, beta, (float)eps, xn, mean, rstd};
     const KernelChoice path = kernel_choice("AIWN_IL_FORWARD", "token", "cluster");
-    if (path != kOnlyOther && il::fast_forward_args_ok(x, x_dtype, table, bias, out, N, IN, OUT, K, c)) {
-        const int rc = il::token_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s);
+    if (path != kOnlyOther && il::fast_forward_args_ok(x, IL_F32, table, bias, out, N, IN, OUT, K, c)) {
+        const int rc = il::token_cdf_forward(x, q, table, bias, out, N, IN, OUT, c, sms, s);
         if (rc != il::kNotApplicable) {
             if (rc) {
                 cudaGetLastError();
@@ -146,32 +209,57 @@ int il_forward(const void* x, int x_dtype, const float* table, const float* bias
             return launch_status();
         }
     }
-    if (path != kOnlyOther && il::fast_forward_args_ok(x, x_dtype, table, bias, out, N, IN, OUT, K, c)) {
-        // tables too large to keep resident: stream column chunks through shared memory
-        const int rc = il::stream_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, s);
-        if (rc != il::kNotApplicable) {
-            if (rc) {
-                cudaGetLastError();
-                return IL_ERR_LAUNCH;
-            }
-            return launch_status();
-        }
-    }
-    if (path != kOnlyPreferred && il::fast_forward_ok(x, x_dtype, table, bias, out, N, IN, OUT, K, c)) {
-        const int rc = il::fast_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s);
-        if (rc != il::kNotApplicable) {
-            if (rc) {
-                cudaGetLastError();
-                return IL_ERR_LAUNCH;
-            }
-            return launch_status();
-        }
-    }
-    const unsigned g = grid_for(N * OUT, 256, sms);
-    if (x_dtype == IL_BF16)
-        il::fwd_simple_kernel<il::kBF16><<<g, 256, 0, s>>>(x, table, bias, out, N, IN, OUT, c);
+    // prologue as its own pass, then the forward on xn
+    const unsigned blocks = (unsigned)((N + il::kCdfRowThreads - 1) / il::kCdfRowThreads);
+    const int vec = (IN % 4 == 0) && ((((uintptr_t)x | (uintptr_t)xn) & 15) == 0);
+    if (IN <= 8)
+        il::cdf_prologue_small_kernel<8><<<blocks, il::kCdfRowThreads, 0, s>>>(x, q, (int)N, (int)IN, vec);
+    else if (IN <= 16)
+        il::cdf_prologue_small_kernel<16><<<blocks, il::kCdfRowThreads, 0, s>>>(x, q, (int)N, (int)IN, vec);
+    else if (IN <= 24)
+        il::cdf_prologue_small_kernel<24><<<blocks, il::kCdfRowThreads, 0, s>>>(x, q, (int)N, (int)IN, vec);
+    else if (IN <= 32)
+        il::cdf_prologue_small_kernel<32><<<blocks, il::kCdfRowThreads, 0, s>>>(x, q, (int)N, (int)IN, vec);
     else
-        il::fwd_simple_kernel<il::kF32><<<g, 256, 0, s>>>(x, table, bias, out, N, IN, OUT, c);
+        il::cdf_prologue_kernel<<<blocks, il::kCdfRowThreads, 0, s>>>(x, q, (int)N, (int)IN);
+    if ((st = launch_status())) return st;
+    return forward_dispatch(xn, IL_F32, table, bias, out, N, IN, OUT, c, sms, s);
+}
+
+int il_cdf_backward(const float* gxn, const float* x, const float* gamma, const float* beta, const float* mean,
+                    const float* rstd, float* dx, float* dgamma, float* dbeta, int64_t N, int64_t IN, void* stream) {
+    if (N < 0 || IN < 1 || IN > 16384 || N > INT32_MAX) return IL_ERR_SHAPE;
+    if (N > 0 && (!gxn || !x || !gamma || !beta || !mean || !rstd)) return IL_ERR_NULL;
+    int sms = 0;
+    int st = check_device(&sms);
+    if (st) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (dgamma && cudaMemsetAsync(dgamma, 0, (size_t)IN * sizeof(float), s) != cudaSuccess) return IL_ERR_LAUNCH;
+    if (dbeta && cudaMemsetAsync(dbeta, 0, (size_t)IN * sizeof(float), s) != cudaSuccess) return IL_ERR_LAUNCH;
+    if (N == 0 || (!dx && !dgamma && !dbeta)) return IL_OK;
+    if (IN <= il::kCdfMaxIn) {
+        const int vec = (IN % 4 == 0) && ((((uintptr_t)gxn | (uintptr_t)x | (uintptr_t)dx) & 15) == 0);
+        // one wave, several tokens per thread: the block reduction runs once per block
+        const int64_t want = (N + il::kCdfRowThreads - 1) / il::kCdfRowThreads;
+        const unsigned blocks = (unsigned)std::min<int64_t>(want, (int64_t)sms);
+        auto run = [&](auto kern) {
+            kern<<<blocks, il::kCdfRowThreads, 0, s>>>(gxn, x, gamma, beta, mean, rstd, dx, dgamma, dbeta, (int)N,
+                                                       (int)IN, vec);
+        };
+        if (IN <= 8) run(il::cdf_backward_small_kernel<8>);
+        else if (IN <= 16) run(il::cdf_backward_small_kernel<16>);
+        else if (IN <= 24) run(il::cdf_backward_small_kernel<24>);
+        else run(il::cdf_backward_small_kernel<32>);
+        return launch_status();
+    }
+    const size_t smem = (size_t)(2 * IN) * sizeof(float);
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(il::cdf_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+        return IL_ERR_LAUNCH;
+    const unsigned blocks = (unsigned)((N + il::kCdfRowThreads - 1) / il::kCdfRowThreads);
+    il::cdf_backward_kernel<<<blocks, il::kCdfRowThreads, smem, s>>>(gxn, x, gamma, beta, mean, rstd, dx, dgamma,
+                                                                      dbeta, (int)N, (int)IN);
     return launch_status();
 }
 

@@ -45,6 +45,9 @@ CONFIGS = {
                   d=512, K=512, B=32, seq=4096, IN=20, OUT=80, xdist="uniform", dtype="f32"),
     "c4": dict(desc="IndexedLinear(1024, 1024, K=64), 16384 tokens per GPU, x=clamp(N(0,0.5)) fp32",
                d=1024, K=64, B=2, seq=8192, IN=1024, OUT=1024, xdist="clamp_normal", dtype="f32"),
+    "c3v2": dict(desc="IndexedLinearV2(20, 20, K=512): GaussianCDFNorm prologue fused into the forward, "
+                      "fwd+bwd, d=512 B=32 seq=4096, x~N(0.3, 1.7^2) fp32", d=512, K=512, B=32, seq=4096, IN=20,
+                 OUT=20, xdist="normal", dtype="f32", v2=True),
     "c5": dict(desc="IndexedGPT projection shape IndexedLinear(16, 16, K=128), batch 64 x ctx 256 "
                     "(16384 tokens), x~U(-1,1) fp32", d=256, K=128, B=64, seq=256, IN=16, OUT=16,
                xdist="uniform", dtype="f32"),
@@ -72,6 +75,8 @@ def make_x(N, IN, xdist, dtype, gen, device):
         x = torch.rand(N, IN, generator=gen, device=device) * 2 - 1
     elif xdist == "tanh_normal":
         x = torch.tanh(torch.randn(N, IN, generator=gen, device=device))
+    elif xdist == "normal":
+        x = torch.randn(N, IN, generator=gen, device=device) * 1.7 + 0.3
     else:
         x = (torch.randn(N, IN, generator=gen, device=device) * 0.5).clamp(-1, 1)
     return x.to(torch.bfloat16) if dtype == "bf16" else x
@@ -145,23 +150,35 @@ def dist_setup(args):
 # reference arm: the reference's eager CPU path on the host cores
 # ---------------------------------------------------------------------------
 
+def cpu_step_fn(cfg, g):
+    """The reference's CPU fwd+bwd step for this config (its eager ops,
+    restated in oracle/eager_port.py): IndexedLinear, or IndexedLinearV2."""
+    from oracle.eager_port import eager_step, eager_step_v2
+    IN, OUT, K = cfg["IN"], cfg["OUT"], cfg["K"]
+    bw = 2.0 / K
+    table = torch.randn(K, IN, OUT, generator=g) / math.sqrt(IN)
+    bias = torch.zeros(OUT)
+    if cfg.get("v2"):
+        gamma = 1.0 + 0.1 * torch.randn(IN, generator=g)
+        beta = 0.1 * torch.randn(IN, generator=g)
+        return lambda x, go: eager_step_v2(x, gamma, beta, 1e-5, table, bias, go, bw)
+    return lambda x, go: eager_step(x, table, bias, go, bw)
+
+
 def run_reference(args, cfg, world, rank):
     if rank != 0:
         return None
-    from oracle.eager_port import eager_step
     torch.set_num_threads(os.cpu_count() or 1)
     N, IN, OUT, K = cfg["B"] * cfg["seq"], cfg["IN"], cfg["OUT"], cfg["K"]
-    bw = 2.0 / K
     g = torch.Generator().manual_seed(0)
-    table = torch.randn(K, IN, OUT, generator=g) / math.sqrt(IN)
-    bias = torch.zeros(OUT)
+    step = cpu_step_fn(cfg, g)
     # size the per-step token sample so the whole run stays within ~2 minutes
     probe = 1024
     x = make_x(probe, IN, cfg["xdist"], cfg["dtype"], g, "cpu")
     go = torch.randn(probe, OUT, generator=g)
-    eager_step(x, table, bias, go, bw)
+    step(x, go)
     t = time.perf_counter()
-    eager_step(x, table, bias, go, bw)
+    step(x, go)
     per_tok = (time.perf_counter() - t) / probe
     budget = 100.0 / max(1, args.steps + args.warmup)
     n_s = int(min(N, max(256, budget / max(per_tok, 1e-12))))
@@ -169,10 +186,10 @@ def run_reference(args, cfg, world, rank):
     x = make_x(n_s, IN, cfg["xdist"], cfg["dtype"], g, "cpu")
     go = torch.randn(n_s, OUT, generator=g)
     for _ in range(args.warmup):
-        eager_step(x, table, bias, go, bw)
+        step(x, go)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        eager_step(x, table, bias, go, bw)
+        step(x, go)
     dt = (time.perf_counter() - t0) / args.steps
     v = n_s / dt
     cores = torch.get_num_threads()
@@ -192,25 +209,22 @@ def run_reference(args, cfg, world, rank):
 
 def cpu_baseline(cfg, seconds=12.0):
     """The reference's CPU path on a bounded sample of the workload."""
-    from oracle.eager_port import eager_step
     torch.set_num_threads(os.cpu_count() or 1)
-    IN, OUT, K = cfg["IN"], cfg["OUT"], cfg["K"]
-    bw = 2.0 / K
+    IN, OUT = cfg["IN"], cfg["OUT"]
     g = torch.Generator().manual_seed(0)
-    table = torch.randn(K, IN, OUT, generator=g) / math.sqrt(IN)
-    bias = torch.zeros(OUT)
+    step = cpu_step_fn(cfg, g)
     n_s = 4096 if IN * OUT <= 4096 else 32
     x = make_x(n_s, IN, cfg["xdist"], cfg["dtype"], g, "cpu")
     go = torch.randn(n_s, OUT, generator=g)
-    eager_step(x, table, bias, go, bw)
+    step(x, go)
     done, t0 = 0, time.perf_counter()
     while time.perf_counter() - t0 < seconds:
-        eager_step(x, table, bias, go, bw)
+        step(x, go)
         done += 1
     dt = (time.perf_counter() - t0) / done
     cores = torch.get_num_threads()
     return {"value": n_s / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{done} fwd+bwd steps of {n_s} tokens (reference eager ops, "
+            "sample": f"{done} fwd+bwd steps of {n_s} tokens (reference eager ops{', V2 chain' if cfg.get('v2') else ''}, "
                       f"oracle/eager_port.py) in {seconds:.0f} s on {cores} threads"}
 
 
@@ -218,7 +232,160 @@ def cpu_baseline(cfg, seconds=12.0):
 # our arm
 # ---------------------------------------------------------------------------
 
+def v2_bytes(N, IN, OUT, K):
+    """Compulsory HBM bytes of IndexedLinearV2: the forward reads x, writes xn,
+    mean, rstd and out; the backward reads go, xn, x, mean, rstd and writes
+    gxn (read back), dx, dtable, dbias, dgamma, dbeta."""
+    tab = K * IN * OUT * 4
+    fwd = N * IN * 4 * 2 + N * 8 + N * OUT * 4 + tab + OUT * 4 + IN * 8
+    bwd = N * OUT * 4 + N * IN * 4 + tab + N * IN * 4 * 2 + tab + OUT * 4 + N * IN * 4 * 2 + N * 8 + IN * 8
+    return fwd, bwd
+
+
+def run_ours_v2(args, cfg, world, rank, local):
+    """IndexedLinearV2: fused prologue + forward, sorted backward on xn, prologue backward."""
+    from aiwn_b200 import IndexedLinearV2, _lib
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    N, IN, OUT, K = cfg["B"] * cfg["seq"], cfg["IN"], cfg["OUT"], cfg["K"]
+    bw = 2.0 / K
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    per_set = N * IN * 4 * 3 + N * OUT * 4 * 2
+    n_sets = max(2, min(16, math.ceil(2 * L2_BYTES / per_set)))
+    xs = [make_x(N, IN, cfg["xdist"], "f32", gen, dev) for _ in range(n_sets)]
+    gos = [torch.randn(N, OUT, generator=gen, device=dev) for _ in range(n_sets)]
+    outs = [torch.empty(N, OUT, device=dev) for _ in range(n_sets)]
+    xns = [torch.empty(N, IN, device=dev) for _ in range(n_sets)]
+    dxs = [torch.empty(N, IN, device=dev) for _ in range(n_sets)]
+    gxn = torch.empty(N, IN, device=dev)
+    mean, rstd = torch.empty(N, device=dev), torch.empty(N, device=dev)
+    table = torch.randn(K, IN, OUT, generator=gen, device=dev) / math.sqrt(IN)
+    gamma = 1.0 + 0.1 * torch.randn(IN, generator=gen, device=dev)
+    beta = 0.1 * torch.randn(IN, generator=gen, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        for t in (table, gamma, beta):
+            dist.broadcast(t, 0)
+    bias = torch.zeros(OUT, device=dev)
+    nb = K * IN * OUT + OUT + 2 * IN
+    bucket = torch.empty(nb, device=dev)  # [dtable | dbias | dgamma | dbeta]
+    gt = bucket[: K * IN * OUT].view(K, IN, OUT)
+    gb = bucket[K * IN * OUT: K * IN * OUT + OUT]
+    dg = bucket[K * IN * OUT + OUT: K * IN * OUT + OUT + IN]
+    db = bucket[K * IN * OUT + OUT + IN:]
+
+    def fwd(i):
+        _lib.cdf_forward(xs[i], gamma, beta, 1e-5, table, bias, xns[i], mean, rstd, outs[i], bw)
+
+    def bwd(i):
+        _lib.backward(gos[i], xns[i], table, gxn, gt, gb, bw)
+        _lib.cdf_backward(gxn, xs[i], gamma, beta, mean, rstd, dxs[i], dg, db)
+
+    def step(k):
+        i = k % n_sets
+        fwd(i)
+        bwd(i)
+        if world > 1:
+            torch.distributed.all_reduce(bucket)
+
+    def sync_all():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def time_calls(fn, reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        sync_all()
+        e0.record()
+        for k in range(reps):
+            fn(k)
+        e1.record()
+        sync_all()
+        return max_over_ranks(e0.elapsed_time(e1) / reps)
+
+    clocks = ClockSampler(local) if rank == 0 else None
+    for k in range(max(3, args.warmup)):
+        step(k)
+    sync_all()
+    if clocks:
+        clocks.start()
+    launches0 = _lib.kernel_launches()
+    ms_step = time_calls(step, args.steps)
+    launches = _lib.kernel_launches() - launches0
+    reps = max(args.steps, 20)
+    ms_fwd = time_calls(lambda k: fwd(k % n_sets), reps)
+    ms_bwd = time_calls(lambda k: (fwd(k % n_sets), bwd(k % n_sets)), reps) - ms_fwd
+
+    # end to end through the module: pinned host x / go in, out / dx out
+    m = IndexedLinearV2(IN, OUT, K).to(dev)
+    with torch.no_grad():
+        m.linear.table.copy_(table)
+        m.cdf.ln.weight.copy_(gamma)
+        m.cdf.ln.bias.copy_(beta)
+    xh = [x.cpu().pin_memory() for x in xs[:2]]
+    goh = [g.cpu().pin_memory() for g in gos[:2]]
+    outh = [torch.empty(N, OUT).pin_memory() for _ in range(2)]
+    dxh = [torch.empty(N, IN).pin_memory() for _ in range(2)]
+
+    def e2e_step(k):
+        i = k % 2
+        m.zero_grad(set_to_none=False)
+        xd = xh[i].to(dev, non_blocking=True).requires_grad_(True)
+        y = m(xd)
+        y.backward(goh[i].to(dev, non_blocking=True))
+        if world > 1:
+            for p_ in m.parameters():
+                torch.distributed.all_reduce(p_.grad)
+        outh[i].copy_(y.detach(), non_blocking=True)
+        dxh[i].copy_(xd.grad, non_blocking=True)
+
+    for k in range(3):
+        e2e_step(k)
+    ms_e2e = time_calls(e2e_step, max(10, min(args.steps, 100)))
+    clk = clocks.stop() if clocks else None
+    if rank != 0:
+        return None
+    hbm, peak_kind = peaks()
+    b_fwd, b_bwd = v2_bytes(N, IN, OUT, K)
+    dom = ("forward", ms_fwd, b_fwd) if ms_fwd >= ms_bwd else ("backward", ms_bwd, b_bwd)
+    achieved = dom[2] / (dom[1] * 1e-3) / 1e9
+    res = {
+        "metric": METRIC, "value": world * N / (ms_step * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cfg["desc"], "K": K, "in_d": IN, "out_d": OUT, "tokens_per_gpu": N, "d": cfg["d"],
+                   "B": cfg["B"], "seq": cfg["seq"], "x_dtype": "f32",
+                   "parallelism": f"token-parallel dp{world}" + (" + NCCL all-reduce of the gradients" if world > 1 else ""),
+                   "l2": f"inputs rotate over {n_sets} sets ({n_sets * per_set / 2**20:.0f} MiB > L2)"},
+        "fwd_tokens_per_s": world * N / (ms_fwd * 1e-3),
+        "fwd_bwd_tokens_per_s": world * N / (ms_step * 1e-3),
+        "ms": {"fwd": ms_fwd, "bwd": ms_bwd, "fwd_bwd": ms_step},
+        "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "traffic": None, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": dom[2]},
+        "e2e": {"value": world * N / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": N * (IN + OUT) * 4,
+                "d2h_bytes_per_step": N * (IN + OUT) * 4,
+                "api": "aiwn_b200.IndexedLinearV2 forward+backward through autograd; pinned host x/go copied in, "
+                       "out/dx copied back each step"},
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(cfg)
+    return res
+
+
 def run_ours(args, cfg, world, rank, local):
+    if cfg.get("v2"):
+        return run_ours_v2(args, cfg, world, rank, local)
     from aiwn_b200 import IndexedLinear, _lib
     from aiwn_b200.distributed import TokenParallelIndexedLinear
     from aiwn_b200.pipeline import HostPipeline

@@ -117,6 +117,29 @@ IL_API int il_adam_step(float* p, const float* g, float* m, float* v, int64_t n,
                  double beta2, double eps, int64_t step, void* stream);
 
 /*
+ * IndexedLinearV2 forward: the GaussianCDFNorm prologue
+ *   xn = 2 * (0.5 * (1 + erf(LayerNorm(x; gamma, beta, eps) / sqrt 2))) - 1
+ * feeding the IndexedLinear forward, out = IndexedLinear(xn).  x is fp32
+ * [N, IN]; gamma, beta [IN].  Also writes xn [N, IN] and the per-token mean
+ * and rstd = 1/sqrt(var + eps) [N], which il_cdf_backward and il_backward (on
+ * xn) need.  For IN <= 32 the prologue runs inside the forward kernel.
+ * Replaces aiwn/layers/indexed_linear_v2.py:19-37 and :80-88.
+ */
+IL_API int il_cdf_forward(const float* x, const float* gamma, const float* beta, double eps, const float* table,
+                   const float* bias, float* xn, float* mean, float* rstd, float* out, int64_t N, int64_t IN,
+                   int64_t OUT, int64_t K, double bw, void* stream);
+
+/*
+ * Backward of the GaussianCDFNorm prologue: given gxn = dL/dxn (from
+ * il_backward run on xn), writes dx [N, IN] and overwrites dgamma, dbeta [IN].
+ * Any of dx / dgamma / dbeta may be NULL.  IN <= 16384.  PyTorch autograd's
+ * backward of aiwn/layers/indexed_linear_v2.py:33-36.
+ */
+IL_API int il_cdf_backward(const float* gxn, const float* x, const float* gamma, const float* beta,
+                    const float* mean, const float* rstd, float* dx, float* dgamma, float* dbeta, int64_t N,
+                    int64_t IN, void* stream);
+
+/*
  * Number of kernels this library has launched in the process so far
  * (host-side counter, all devices and threads).  Lets a caller count the
  * library's launches inside a timed region.

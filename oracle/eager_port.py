@@ -12,6 +12,8 @@ The parity checker is the C oracle (``oracle/il_oracle.c``).
 """
 from __future__ import annotations
 
+import math
+
 import torch
 
 
@@ -32,5 +34,24 @@ def eager_step(x, table, bias, go, bw):
     tl = table.detach().requires_grad_(True)
     bl = bias.detach().requires_grad_(True)
     out = eager_forward(xl, tl, bl, bw)
+    out.backward(go)
+    return out.detach(), xl.grad, tl.grad, bl.grad
+
+
+def eager_cdf_norm(x, gamma, beta, eps):
+    """GaussianCDFNorm.forward (aiwn/layers/indexed_linear_v2.py:33-36), same ATen ops."""
+    z = torch.nn.functional.layer_norm(x, (x.shape[-1],), gamma, beta, eps)
+    u = 0.5 * (1.0 + torch.erf(z / math.sqrt(2.0)))
+    return u * 2.0 - 1.0
+
+
+def eager_step_v2(x, gamma, beta, eps, table, bias, go, bw):
+    """fwd + bwd of IndexedLinearV2's CPU path (prologue, then _eager)."""
+    xl = x.detach().requires_grad_(True)
+    gl = gamma.detach().requires_grad_(True)
+    bl_ = beta.detach().requires_grad_(True)
+    tl = table.detach().requires_grad_(True)
+    bl = bias.detach().requires_grad_(True)
+    out = eager_forward(eager_cdf_norm(xl, gl, bl_, eps), tl, bl, bw)
     out.backward(go)
     return out.detach(), xl.grad, tl.grad, bl.grad

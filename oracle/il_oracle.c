@@ -35,6 +35,15 @@
  *     INT64_MIN on x86 (cvttss2si), which the clamp turns into bin 0.
  *   - clamp propagates NaN; its gradient passes where min <= v <= max.
  *
+ * GaussianCDFNorm prologue of IndexedLinearV2 (aiwn/layers/indexed_linear_v2.py:19-37):
+ *   z = LayerNorm(x) (biased variance, eps), e = erf(z / sqrt 2),
+ *   u = 0.5 * (1 + e), xn = u * 2 - 1, each fp32 operation rounded once; the
+ *   row mean and variance are accumulated in double (closest to ATen's
+ *   vectorised moments; the restatement stays within 2.4e-7 of the
+ *   reference).  erf is the C library's erff.  Its backward is autograd's:
+ *   ds = g * 2/sqrt(pi) * exp(-s^2) with s = z / sqrt 2, dz = ds / sqrt 2,
+ *   then ATen's LayerNorm backward.
+ *
  * Build: oracle/Makefile  (gcc -O2 -ffp-contract=off: no FMA contraction,
  * every fp32 operation rounds exactly once, as ATen's elementwise ops do).
  */
@@ -334,4 +343,83 @@ void il_oracle_adam(float* p, const float* g, float* m, float* v, int64_t n, dou
         float denom = sqrtf(v[k]) / bc2_sqrt + e;
         p[k] = p[k] - step_size * (m[k] / denom);
     }
+}
+
+
+/* ---- GaussianCDFNorm prologue (IndexedLinearV2) --------------------------- */
+
+static const float kSqrt2f = 1.41421354f; /* fp32 value of math.sqrt(2.0) */
+
+static void row_moments(const float* r, int64_t IN, float eps, float* mean, float* rstd) {
+    double s = 0.0, q = 0.0;
+    for (int64_t k = 0; k < IN; ++k) s += r[k];
+    const double m = s / (double)IN;
+    for (int64_t k = 0; k < IN; ++k) q += ((double)r[k] - m) * ((double)r[k] - m);
+    *mean = (float)m;
+    const float var = (float)(q / (double)IN);
+    *rstd = 1.0f / sqrtf(var + eps);
+}
+
+/* xn [N, IN], mean [N], rstd [N]  (aiwn/layers/indexed_linear_v2.py:33-36) */
+void il_oracle_cdf_forward(const float* x, const float* gamma, const float* beta, double eps, int64_t N,
+                           int64_t IN, float* xn, float* mean, float* rstd) {
+    const float epsf = (float)eps;
+    for (int64_t n = 0; n < N; ++n) {
+        const float* r = x + n * IN;
+        float m, rs;
+        row_moments(r, IN, epsf, &m, &rs);
+        if (mean) mean[n] = m;
+        if (rstd) rstd[n] = rs;
+        for (int64_t k = 0; k < IN; ++k) {
+            const float z = ((r[k] - m) * rs) * gamma[k] + beta[k];
+            const float e = erff(z / kSqrt2f);
+            const float u = 0.5f * (1.0f + e);
+            xn[n * IN + k] = u * 2.0f - 1.0f;
+        }
+    }
+}
+
+/* dx [N, IN], dgamma [IN], dbeta [IN] given g = dL/dxn (any output may be NULL) */
+int il_oracle_cdf_backward(const float* g, const float* x, const float* gamma, const float* beta, double eps,
+                           int64_t N, int64_t IN, float* dx, float* dgamma, float* dbeta) {
+    const float epsf = (float)eps;
+    double* ag = (double*)calloc((size_t)(2 * IN), sizeof(double));
+    float* dz = (float*)malloc((size_t)IN * sizeof(float));
+    if (!ag || !dz) {
+        free(ag);
+        free(dz);
+        return 1;
+    }
+    for (int64_t n = 0; n < N; ++n) {
+        const float* r = x + n * IN;
+        float m, rs;
+        row_moments(r, IN, epsf, &m, &rs);
+        double sdy_g_x = 0.0, sdy_g = 0.0;
+        for (int64_t k = 0; k < IN; ++k) {
+            const float xh = (r[k] - m) * rs;
+            const float z = xh * gamma[k] + beta[k];
+            const float sv = z / kSqrt2f;
+            const float ds = (g[n * IN + k] * 1.12837916709551257f) * expf(-(sv * sv));
+            dz[k] = ds / kSqrt2f;
+            ag[k] += (double)dz[k] * (double)xh;
+            ag[IN + k] += (double)dz[k];
+            sdy_g_x += (double)dz[k] * (double)gamma[k] * (double)r[k];
+            sdy_g += (double)dz[k] * (double)gamma[k];
+        }
+        if (dx) {
+            /* ATen's CPU LayerNorm backward: dx = a*dy*gamma + b*x + c */
+            const double a = rs;
+            const double b = (sdy_g * m - sdy_g_x) * a * a * a / (double)IN;
+            const double c = -b * m - sdy_g * a / (double)IN;
+            for (int64_t k = 0; k < IN; ++k)
+                dx[n * IN + k] = (float)(a * (double)dz[k] * (double)gamma[k] + b * (double)r[k] + c);
+        }
+    }
+    for (int64_t k = 0; k < IN; ++k) {
+        if (dgamma) dgamma[k] = (float)ag[k];
+        if (dbeta) dbeta[k] = (float)ag[IN + k];
+    }
+    free(ag);
+    free(dz);
+    return 0;
 }

@@ -49,6 +49,10 @@ def _load():
         lib.il_oracle_forward.restype = None
         lib.il_oracle_backward.argtypes = [vp, vp, ci, vp, vp, vp, vp, i64, i64, i64, i64, f64, ci]
         lib.il_oracle_backward.restype = ci
+        lib.il_oracle_cdf_forward.argtypes = [vp, vp, vp, f64, i64, i64, vp, vp, vp]
+        lib.il_oracle_cdf_forward.restype = None
+        lib.il_oracle_cdf_backward.argtypes = [vp, vp, vp, vp, f64, i64, i64, vp, vp, vp]
+        lib.il_oracle_cdf_backward.restype = ci
         lib.il_oracle_adam.argtypes = [vp, vp, vp, vp, i64, f64, f64, f64, f64, i64]
         lib.il_oracle_adam.restype = None
         _lib = lib
@@ -112,6 +116,37 @@ def backward(go, x, table, bw: float, x_dtype: str = "f32", nthreads: int = 0,
     if rc != 0:
         raise MemoryError("oracle backward: allocation failed")
     return gx, gt, gb
+
+
+def cdf_forward(x, gamma, beta, eps: float):
+    """(xn, mean, rstd) of the GaussianCDFNorm prologue
+    (aiwn/layers/indexed_linear_v2.py:19-37), fp32."""
+    x = _c(x, np.float32)
+    gamma = _c(gamma, np.float32)
+    beta = _c(beta, np.float32)
+    N, IN = x.shape
+    xn = np.empty_like(x)
+    mean = np.empty(N, np.float32)
+    rstd = np.empty(N, np.float32)
+    _load().il_oracle_cdf_forward(_ptr(x), _ptr(gamma), _ptr(beta), eps, N, IN, _ptr(xn), _ptr(mean), _ptr(rstd))
+    return xn, mean, rstd
+
+
+def cdf_backward(g, x, gamma, beta, eps: float):
+    """(dx, dgamma, dbeta): autograd's backward of the prologue given g = dL/dxn."""
+    g = _c(g, np.float32)
+    x = _c(x, np.float32)
+    gamma = _c(gamma, np.float32)
+    beta = _c(beta, np.float32)
+    N, IN = x.shape
+    dx = np.empty_like(x)
+    dgamma = np.empty(IN, np.float32)
+    dbeta = np.empty(IN, np.float32)
+    rc = _load().il_oracle_cdf_backward(_ptr(g), _ptr(x), _ptr(gamma), _ptr(beta), eps, N, IN, _ptr(dx),
+                                        _ptr(dgamma), _ptr(dbeta))
+    if rc != 0:
+        raise MemoryError("oracle cdf backward: allocation failed")
+    return dx, dgamma, dbeta
 
 
 def adam(p, g, m, v, lr, beta1, beta2, eps, step):

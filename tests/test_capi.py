@@ -72,3 +72,19 @@ def test_adam_argument_checks():
 def test_workspace_query_is_host_only():
     n = _lib.workspace_bytes(131072, 20, 20, 512, 0)
     assert n >= 0
+
+
+def test_cdf_entry_points_argument_checks():
+    """il_cdf_forward / il_cdf_backward reject bad arguments before touching a device."""
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    # empty batch: nothing to do
+    assert lib.il_cdf_forward(None, None, None, 1e-5, None, None, None, None, None, None, 0, 4, 4, 8, 0.25,
+                              None) == 0
+    # NULL gamma with N > 0, negative eps, bad K
+    assert lib.il_cdf_forward(p, None, p, 1e-5, p, p, p, p, p, p, 4, 4, 4, 8, 0.25, None) == 6
+    assert lib.il_cdf_forward(p, p, p, -1.0, p, p, p, p, p, p, 4, 4, 4, 8, 0.25, None) == 9
+    assert lib.il_cdf_forward(p, p, p, 1e-5, p, p, p, p, p, p, 4, 4, 4, 1, 0.25, None) == 1
+    # in_d beyond the backward's per-block shared-memory sums, NULL inputs
+    assert lib.il_cdf_backward(p, p, p, p, p, p, p, p, p, 4, 20000, None) == 1
+    assert lib.il_cdf_backward(None, p, p, p, p, p, p, p, p, 4, 8, None) == 6

@@ -48,3 +48,33 @@ def test_oracle_threads_deterministic():
     g4 = oracle.backward(d["go"], d["x"], d["table"], d["bw"], nthreads=4)
     for u, v in zip(g1, g4):
         assert np.array_equal(u, v)
+
+
+# ---- IndexedLinearV2: the GaussianCDFNorm prologue ---------------------------
+
+CDF_CASES = ["cdfnorm_20x20_k64", "cdfnorm_16x8_k128"]
+XN_ATOL = 1e-6  # LayerNorm moments and erf round differently from ATen's (measured max 2.4e-7)
+
+
+def load_cdf(name):
+    import os
+    return dict(np.load(os.path.join(os.path.dirname(__file__), "golden", f"{name}.npz")))
+
+
+@pytest.mark.parametrize("name", CDF_CASES)
+def test_oracle_cdfnorm_chain(name):
+    """Prologue, IndexedLinear on xn and the prologue's backward, each against
+    the reference's own values (tests/golden/make_golden_cdfnorm.py)."""
+    d = load_cdf(name)
+    eps, bw = float(d["eps"]), float(d["bw"])
+    xn, _, _ = oracle.cdf_forward(d["x"], d["gamma"], d["beta"], eps)
+    assert np.abs(xn - d["xn"]).max() <= XN_ATOL
+    normwise_close(oracle.forward(d["xn"], d["table"], d["bias"], bw), d["out"], FWD_RTOL, "out")
+    gxn, gt, gb = oracle.backward(d["go"], d["xn"], d["table"], bw)
+    normwise_close(gxn, d["gxn"], GRAD_RTOL, "gxn")
+    normwise_close(gt, d["gt"], GRAD_RTOL, "gt")
+    normwise_close(gb, d["gb"], GRAD_RTOL, "gb")
+    dx, dg, db = oracle.cdf_backward(d["gxn"], d["x"], d["gamma"], d["beta"], eps)
+    normwise_close(dx, d["gx"], GRAD_RTOL, "dx")
+    normwise_close(dg, d["ggamma"], GRAD_RTOL, "dgamma")
+    normwise_close(db, d["gbeta"], GRAD_RTOL, "dbeta")
