@@ -58,6 +58,8 @@ def load():
         lib.il_cdf_forward.restype = ci
         lib.il_cdf_backward.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
         lib.il_cdf_backward.restype = ci
+        lib.il_bin_counts.argtypes = [vp, ci, i64, i64, i64, f64, vp, vp]
+        lib.il_bin_counts.restype = ci
         lib.il_kernel_launches.argtypes = []
         lib.il_kernel_launches.restype = i64
         lib.il_check_device_status.argtypes = [vp]
@@ -179,6 +181,19 @@ def cdf_backward(gxn, x, gamma, beta, mean, rstd, dx, dgamma, dbeta):
     with _on_device(x.device):
         _check(lib.il_cdf_backward(_p(gxn), _p(x), _p(gamma), _p(beta), _p(mean), _p(rstd), _p(dx), _p(dgamma),
                                    _p(dbeta), N, IN, _stream(x.device)), "il_cdf_backward")
+
+
+def bin_counts(x, K: int, bw: float, counts):
+    """counts[K] (int64, device) += occupancy of the bins of x[..., IN]."""
+    _need_cuda(x, counts)
+    if counts.dtype != torch.int64 or counts.numel() != K:
+        raise ILError("bin_counts needs an int64 counts tensor of K elements")
+    x2 = x.reshape(-1, x.shape[-1])
+    lib = load()
+    with _on_device(x.device):
+        _check(lib.il_bin_counts(_p(x2), x_dtype_code(x2), x2.shape[0], x2.shape[1], K, float(bw), _p(counts),
+                                 _stream(x.device)), "il_bin_counts")
+    return counts
 
 
 def bins(x, K: int, bw: float):

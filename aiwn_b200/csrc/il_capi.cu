@@ -352,6 +352,27 @@ int il_bins(const void* x, int x_dtype, int64_t N, int64_t IN, int64_t K, double
     return launch_status();
 }
 
+int il_bin_counts(const void* x, int x_dtype, int64_t N, int64_t IN, int64_t K, double bw, uint64_t* counts,
+                  void* stream) {
+    int st = check_common(x, x_dtype, N, IN, K, bw);
+    if (st) return st;
+    if (K > 16384) return IL_ERR_SHAPE;  // per-CTA counters live in shared memory
+    if (N == 0) return IL_OK;
+    if (!counts) return IL_ERR_NULL;
+    int sms = 0;
+    if ((st = check_device(&sms))) return st;
+    const il::BinCfg c = make_cfg(bw, K);
+    const unsigned g = grid_for(N * IN, 256, sms);
+    cudaStream_t s = (cudaStream_t)stream;
+    const size_t smem = (size_t)K * sizeof(unsigned int);
+    auto* cnt = reinterpret_cast<unsigned long long*>(counts);
+    if (x_dtype == IL_BF16)
+        il::bin_counts_kernel<il::kBF16><<<g, 256, smem, s>>>(x, N * IN, c, cnt);
+    else
+        il::bin_counts_kernel<il::kF32><<<g, 256, smem, s>>>(x, N * IN, c, cnt);
+    return launch_status();
+}
+
 int il_adam_step(float* p, const float* g, float* m, float* v, int64_t n, double lr, double beta1,
                  double beta2, double eps, int64_t step, void* stream) {
     if (n < 0 || step < 1) return IL_ERR_SHAPE;

@@ -129,6 +129,24 @@ __global__ void __launch_bounds__(256) bins_kernel(const void* __restrict__ x, i
     }
 }
 
+// Bin-occupancy histogram: counts[k] += number of x elements whose bin lo is
+// k (the bincount of aiwn/experiments/bucket_analysis.py:44-47 and of
+// transformer_validation.py:105-108).  Per-CTA counters in shared memory
+// (dynamic, K entries), one 64-bit atomic per bin and CTA at the end.
+template <int DT>
+__global__ void __launch_bounds__(256) bin_counts_kernel(const void* __restrict__ x, int64_t total, BinCfg c,
+                                                         unsigned long long* __restrict__ counts) {
+    extern __shared__ unsigned int hist[];
+    for (int k = threadIdx.x; k < c.K; k += blockDim.x) hist[k] = 0u;
+    __syncthreads();
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x)
+        atomicAdd(&hist[bin_of<DT>(load_x<DT>(x, e), c).lo], 1u);
+    __syncthreads();
+    for (int k = threadIdx.x; k < c.K; k += blockDim.x)
+        if (hist[k]) atomicAdd(counts + k, (unsigned long long)hist[k]);
+}
+
 // torch.optim.Adam (single-tensor order) in fp32:
 //   m = m + (g - m)*(1-b1);  v = v*b2 + ((1-b2)*g)*g
 //   p = p - step_size * m / (sqrt(v)/bc2_sqrt + eps)

@@ -109,6 +109,15 @@ IL_API int il_bins(const void* x, int x_dtype, int64_t N, int64_t IN, int64_t K,
             int32_t* hi, float* fr, void* stream);
 
 /*
+ * Bin-occupancy histogram: counts[k] += the number of elements of x[N, IN]
+ * whose bin lo is k (k < K <= 16384), with the bit-exact bins of il_bins.
+ * Accumulates, so repeated calls add up.  Replaces the bincount of
+ * aiwn/experiments/bucket_analysis.py:44-47 and transformer_validation.py:105-108.
+ */
+IL_API int il_bin_counts(const void* x, int x_dtype, int64_t N, int64_t IN, int64_t K, double bw,
+                  uint64_t* counts, void* stream);
+
+/*
  * One fused Adam step over `n` fp32 parameters (torch.optim.Adam semantics,
  * no weight decay, no amsgrad):  m = b1 m + (1-b1) g;  v = b2 v + (1-b2) g^2;
  * p -= lr/(1-b1^step) * m / (sqrt(v)/sqrt(1-b2^step) + eps).

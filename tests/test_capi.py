@@ -88,3 +88,12 @@ def test_cdf_entry_points_argument_checks():
     # in_d beyond the backward's per-block shared-memory sums, NULL inputs
     assert lib.il_cdf_backward(p, p, p, p, p, p, p, p, p, 4, 20000, None) == 1
     assert lib.il_cdf_backward(None, p, p, p, p, p, p, p, p, 4, 8, None) == 6
+
+
+def test_bin_counts_argument_checks():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    assert lib.il_bin_counts(None, 0, 0, 4, 8, 0.25, None, None) == 0
+    assert lib.il_bin_counts(p, 0, 4, 4, 8, 0.25, None, None) == 6
+    assert lib.il_bin_counts(p, 0, 4, 4, 20000, 2.0 / 20000, p, None) == 1
+    assert lib.il_bin_counts(p, 5, 4, 4, 8, 0.25, p, None) == 2
