@@ -267,8 +267,8 @@ __global__ void __launch_bounds__(kSrtThreads, kSrtCtasPerSm) bwd_sorted_kernel(
         const int e1 = glive ? min(nt, e0 + per) : nt;
         const int steps = (per + kSrtDepth - 1) / kSrtDepth * kSrtDepth;
         if (p.want_gx && p.gx_atomic) {
-            // only the 128-column j-ranges of OUT > 128 split dx (fp32 x)
-            if constexpr (DT == kF32 && C == 32)
+            // only the power-of-two j-ranges of OUT > 128 split dx (fp32 x)
+            if constexpr (DT == kF32 && (C & (C - 1)) == 0)
                 srt_walk<DT, C, true, true>(p, slice_s, ew_s, en_s, t0, e0, e1, steps, gl, i);
         } else if (p.want_gx) {
             srt_walk<DT, C, true, false>(p, slice_s, ew_s, en_s, t0, e0, e1, steps, gl, i);
@@ -316,15 +316,16 @@ struct SrtPlan {
 constexpr int kSrtChunks[] = {32, 20, 16, 10, 8, 5, 4, 2, 1};
 
 // j-ranges of 4*C output columns: one range when OUT/4 is an instantiated C,
-// else ranges of 128 columns (C = 32) when OUT is a multiple of 128
+// else equal ranges of the widest power-of-two C <= 32 dividing OUT/4
 inline bool plan_sorted(int64_t N, int K, int IN, int OUT, int sms, SrtPlan& pl) {
     if (OUT % 4 != 0 || K < 1 || K > 65535 || IN > 65535) return false;
     if ((int64_t)K * IN * OUT >= ((int64_t)1 << 31)) return false;  // 32-bit gt offsets
     int C = OUT / 4, jranges = 1;
     if (C > 32) {
-        if (OUT % 128 != 0) return false;
-        C = 32;
-        jranges = OUT / 128;
+        int c = 32;
+        while (c > 1 && (OUT / 4) % c != 0) c >>= 1;
+        jranges = (OUT / 4) / c;
+        C = c;
     }
     bool inst = false;
     for (int c : kSrtChunks) inst |= (c == C);

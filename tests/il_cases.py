@@ -50,6 +50,7 @@ EDGE_CASES = [
     Case("k3000_out8", 2000, 3, 8, 3000, "uniform", "f32", 0.3, 29),
     Case("out256_k32_jranges", 700, 6, 256, 32, "wide", "f32", 0.3, 30),
     Case("out256_k64_bf16", 500, 8, 256, 64, "wide", "bf16", 0.3, 31),
+    Case("out176_k32_jranges", 500, 12, 176, 32, "wide", "f32", 0.3, 34),  # 11 j-ranges of 16 columns
     # too large to keep resident: the streamed forward (partial last column chunk, partial token tile)
     Case("stream_in300_out8_k256", 600, 300, 8, 256, "wide", "f32", 0.3, 32),
     Case("stream_in300_out8_k256_bf16", 600, 300, 8, 256, "wide", "bf16", 0.3, 33),
