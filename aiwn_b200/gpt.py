@@ -1,0 +1,232 @@
+"""IndexedGPT on B200 -- the reference's transformer with every projection an
+IndexedLinear (transformer_validation.py:232-385), built on this package's
+layers, and a training step captured as one CUDA graph.
+
+Module structure, parameter names and initialisation follow the reference
+(``transformer.wte / wpe / h[i].{ln1, ln2, attn.{q,k,v,c}_proj, ffn.{cdf,
+up, down}} / ln_f``, ``lm_head``), so its state_dicts load unchanged.  The
+FFN's GaussianCDFNorm -> up pair runs as one IndexedLinearV2 chain
+(``il_cdf_forward``: the prologue fused into the forward when its output fits
+one j-range); every other IndexedLinear runs the library's forward and
+backward kernels.
+
+At the reference's config-5 sizes (n_embd 256, K=128 -> d_idx 16, ff_idx 8;
+batch 64 x ctx 256) every kernel is small and the eager step is bound by
+launch and host overhead.  ``GraphedTrainStep`` captures forward, backward,
+gradient clipping and a capturable AdamW step once and replays them: one
+graph launch per step.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .layers import GaussianCDFNorm, IndexedLinear
+from .layers.indexed_linear import TRITON_OK
+from .layers.indexed_linear_v2 import _FnV2
+
+
+def get_d_idx(n_embd: int, K: int, n_head: int) -> tuple:
+    """(d_idx, ff_idx): n_embd/sqrt(K) and 4*n_embd/K, each rounded down to a
+    power of two (d_idx also divisible by n_head), as transformer_validation.py:68-87."""
+    raw_d = int(n_embd / math.sqrt(K))
+    p2_d = 1 << (raw_d.bit_length() - 1)
+    while p2_d % n_head != 0 and p2_d > n_head:
+        p2_d >>= 1
+    d_idx = max(n_head, p2_d)
+    raw_ff = max(4, (4 * n_embd) // K)
+    p2_ff = 1 << (raw_ff.bit_length() - 1)
+    ff_idx = max(4, p2_ff)
+    return d_idx, ff_idx
+
+
+class IndexedAttention(nn.Module):
+    """Causal multi-head attention with IndexedLinear q/k/v/c projections."""
+
+    def __init__(self, d_idx, n_head, block_size, K, dropout=0.1):
+        super().__init__()
+        assert d_idx % n_head == 0
+        self.n_head = n_head
+        self.d_idx = d_idx
+        self.q_proj = IndexedLinear(d_idx, d_idx, K)
+        self.k_proj = IndexedLinear(d_idx, d_idx, K)
+        self.v_proj = IndexedLinear(d_idx, d_idx, K)
+        self.c_proj = IndexedLinear(d_idx, d_idx, K)
+        self.attn_drop = nn.Dropout(dropout)
+        self.resid_drop = nn.Dropout(dropout)
+        self.register_buffer("bias", torch.tril(torch.ones(block_size, block_size)).view(1, 1, block_size,
+                                                                                          block_size))
+
+    def forward(self, x):
+        B, T, C = x.shape
+        h = x.reshape(B * T, C)
+        q = self.q_proj(h).reshape(B, T, self.d_idx)
+        k = self.k_proj(h).reshape(B, T, self.d_idx)
+        v = self.v_proj(h).reshape(B, T, self.d_idx)
+        k = k.view(B, T, self.n_head, C // self.n_head).transpose(1, 2)
+        q = q.view(B, T, self.n_head, C // self.n_head).transpose(1, 2)
+        v = v.view(B, T, self.n_head, C // self.n_head).transpose(1, 2)
+        att = (q @ k.transpose(-2, -1)) * (1.0 / math.sqrt(k.size(-1)))
+        att = att.masked_fill(self.bias[:, :, :T, :T] == 0, float("-inf"))
+        att = self.attn_drop(F.softmax(att, dim=-1))
+        y = (att @ v).transpose(1, 2).contiguous().view(B, T, C)
+        h = self.c_proj(y.reshape(B * T, C)).reshape(B, T, C)
+        return self.resid_drop(h)
+
+
+class IndexedFFN(nn.Module):
+    """GaussianCDFNorm -> IndexedLinear up -> GELU -> IndexedLinear down."""
+
+    def __init__(self, d_idx, ff_idx, K, dropout=0.1):
+        super().__init__()
+        self.d_idx = d_idx
+        self.ff_idx = ff_idx
+        self.cdf = GaussianCDFNorm(d_idx)
+        self.up = IndexedLinear(d_idx, ff_idx, K)
+        self.down = IndexedLinear(ff_idx, d_idx, K)
+        self.act = nn.GELU()
+        self.drop = nn.Dropout(dropout)
+
+    def forward(self, x):
+        shape = x.shape
+        xf = x.reshape(-1, self.d_idx)
+        if xf.dtype != torch.float32:
+            xf = xf.float()
+        if self.up._forward_pre_hooks or self.up._forward_hooks:
+            h = self.up(self.cdf(xf))  # hooks (e.g. a BucketTracker) see up's input, as in the reference
+        else:
+            ln = self.cdf.ln
+            h = _FnV2.apply(xf, ln.weight, ln.bias, ln.eps, self.up.table, self.up.bias, self.up.bw)
+        h = self.act(h)
+        h = self.down(h)
+        return self.drop(h.reshape(shape))
+
+
+class IndexedBlock(nn.Module):
+    def __init__(self, d_idx, ff_idx, n_head, block_size, K, dropout=0.1):
+        super().__init__()
+        self.ln1 = nn.LayerNorm(d_idx)
+        self.ln2 = nn.LayerNorm(d_idx)
+        self.attn = IndexedAttention(d_idx, n_head, block_size, K, dropout)
+        self.ffn = IndexedFFN(d_idx, ff_idx, K, dropout)
+
+    def forward(self, x):
+        x = x + self.attn(self.ln1(x))
+        x = x + self.ffn(self.ln2(x))
+        return x
+
+
+class IndexedGPT(nn.Module):
+    """GPT with every linear op an IndexedLinear at d_idx (transformer_validation.py:295-385)."""
+
+    def __init__(self, vocab_size, block_size, n_layer, n_head, n_embd, K, dropout=0.1):
+        super().__init__()
+        self.block_size = block_size
+        self.ffn_type = "indexed"
+        self.K = K
+        d_idx, ff_idx = get_d_idx(n_embd, K, n_head)
+        self.d_idx = d_idx
+        self.ff_idx = ff_idx
+        self.transformer = nn.ModuleDict({
+            "wte": nn.Embedding(vocab_size, d_idx),
+            "wpe": nn.Embedding(block_size, d_idx),
+            "drop": nn.Dropout(dropout),
+            "h": nn.ModuleList([IndexedBlock(d_idx, ff_idx, n_head, block_size, K, dropout)
+                                for _ in range(n_layer)]),
+            "ln_f": nn.LayerNorm(d_idx),
+        })
+        self.lm_head = nn.Linear(d_idx, vocab_size, bias=False)
+        self._init_weights()
+        for m in self.modules():
+            if isinstance(m, IndexedLinear):
+                nn.init.normal_(m.table, std=0.01)
+                nn.init.zeros_(m.bias)
+        n = sum(p.numel() for p in self.parameters())
+        print(f"  IndexedGPT: n_embd={n_embd}→d_idx={d_idx} ff_idx={ff_idx} K={K} | "
+              f"{n / 1e6:.2f}M params | Triton={TRITON_OK}")
+
+    def _init_weights(self):
+        for m in self.modules():
+            if isinstance(m, nn.Linear):
+                nn.init.normal_(m.weight, std=0.02)
+                if m.bias is not None:
+                    nn.init.zeros_(m.bias)
+            elif isinstance(m, nn.Embedding):
+                nn.init.normal_(m.weight, std=0.02)
+
+    def forward(self, idx, targets=None):
+        B, T = idx.shape
+        x = self.transformer["drop"](self.transformer["wte"](idx) +
+                                     self.transformer["wpe"](torch.arange(T, device=idx.device)))
+        for block in self.transformer["h"]:
+            x = block(x)
+        x = self.transformer["ln_f"](x)
+        logits = self.lm_head(x)
+        loss = None
+        if targets is not None:
+            loss = F.cross_entropy(logits.view(-1, logits.size(-1)), targets.view(-1))
+        return logits, loss
+
+    def get_indexed_layers(self):
+        layers = []
+        for blk in self.transformer["h"]:
+            layers += [blk.attn.q_proj, blk.attn.k_proj, blk.attn.v_proj, blk.attn.c_proj, blk.ffn.up,
+                       blk.ffn.down]
+        return layers
+
+
+class GraphedTrainStep:
+    """One training step of ``model`` -- forward, loss, backward,
+    clip_grad_norm_(clip), optimizer.step() -- captured once as a CUDA graph
+    for a fixed (batch, ctx) and replayed.
+
+        opt = torch.optim.AdamW(model.parameters(), lr, weight_decay=wd, capturable=True)
+        step = GraphedTrainStep(model, opt, batch, ctx)
+        loss = step(x, y)          # device int64 [batch, ctx]; returns the loss tensor
+
+    The optimizer must be capturable.  Gradients live in the graph's memory
+    pool and are overwritten (not accumulated) every step.  Construction runs
+    ``warmup`` eager steps (on all-zero tokens) so that the optimizer state and
+    the kernels are set up before capture, then puts the parameters back and
+    zeroes the optimizer state: the model is unchanged until the first call.
+    """
+
+    def __init__(self, model, optimizer, batch_size, block_size, clip: float = 1.0, warmup: int = 3):
+        dev = next(model.parameters()).device
+        self.model, self.opt, self.clip = model, optimizer, clip
+        self.x = torch.zeros(batch_size, block_size, dtype=torch.long, device=dev)
+        self.y = torch.zeros(batch_size, block_size, dtype=torch.long, device=dev)
+        saved = [p.detach().clone() for p in model.parameters()]
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):  # warm-up: optimizer state, autograd, kernel set-up
+            for _ in range(warmup):
+                self.opt.zero_grad(set_to_none=True)
+                _, loss = self.model(self.x, self.y)
+                loss.backward()
+                torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.clip)
+                self.opt.step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        with torch.no_grad():
+            for p, v in zip(model.parameters(), saved):
+                p.copy_(v)
+            for st in self.opt.state.values():
+                for v in st.values():
+                    if torch.is_tensor(v):
+                        v.zero_()
+        self.graph = torch.cuda.CUDAGraph()
+        self.opt.zero_grad(set_to_none=True)
+        with torch.cuda.graph(self.graph, capture_error_mode="relaxed"):
+            _, self.loss = self.model(self.x, self.y)
+            self.loss.backward()
+            torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.clip)
+            self.opt.step()
+
+    def __call__(self, x, y):
+        self.x.copy_(x, non_blocking=True)
+        self.y.copy_(y, non_blocking=True)
+        self.graph.replay()
+        return self.loss

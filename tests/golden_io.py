@@ -21,7 +21,7 @@ def seeded_table(K: int, IN: int, OUT: int, seed: int) -> np.ndarray:
 
 def case_names():
     return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
-                  if not os.path.basename(p).startswith(("bins_", "cdfnorm_")))
+                  if not os.path.basename(p).startswith(("bins_", "cdfnorm_", "gpt_")))
 
 
 def bins_names():
