@@ -48,6 +48,9 @@ CONFIGS = {
     "c3v2": dict(desc="IndexedLinearV2(20, 20, K=512): GaussianCDFNorm prologue fused into the forward, "
                       "fwd+bwd, d=512 B=32 seq=4096, x~N(0.3, 1.7^2) fp32", d=512, K=512, B=32, seq=4096, IN=20,
                  OUT=20, xdist="normal", dtype="f32", v2=True),
+    "c5gpt": dict(desc="config 5: IndexedGPT training step (4 layers, n_embd 256 -> d_idx 16, ff_idx 8, 4 heads, "
+                       "K=128, vocab 65, ctx 256, batch 64), fp32, AdamW + clip, CUDA-graph replay",
+                  d=256, K=128, B=64, seq=256, IN=16, OUT=16, xdist="uniform", dtype="f32", gpt=True),
     "c5": dict(desc="IndexedGPT projection shape IndexedLinear(16, 16, K=128), batch 64 x ctx 256 "
                     "(16384 tokens), x~U(-1,1) fp32", d=256, K=128, B=64, seq=256, IN=16, OUT=16,
                xdist="uniform", dtype="f32"),
@@ -168,6 +171,14 @@ def cpu_step_fn(cfg, g):
 def run_reference(args, cfg, world, rank):
     if rank != 0:
         return None
+    if cfg.get("gpt"):
+        b = gpt_cpu_baseline(cfg, seconds=max(5.0, min(60.0, 2.0 * (args.steps + args.warmup))))
+        return {"metric": METRIC, "value": b["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+                "config": {"workload": cfg["desc"], "K": cfg["K"], "tokens_per_gpu": cfg["B"] * cfg["seq"]},
+                "cpu_baseline": b, "e2e": {"value": b["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                           "d2h_bytes_per_step": 0}}
     torch.set_num_threads(os.cpu_count() or 1)
     N, IN, OUT, K = cfg["B"] * cfg["seq"], cfg["IN"], cfg["OUT"], cfg["K"]
     g = torch.Generator().manual_seed(0)
@@ -383,7 +394,174 @@ def run_ours_v2(args, cfg, world, rank, local):
     return res
 
 
+GPT_CFG = dict(vocab_size=65, block_size=256, n_layer=4, n_head=4, n_embd=256, K=128, dropout=0.1)
+
+
+def _zipf_tokens(n, vocab, gen, device):
+    """Seeded synthetic token stream: Zipf(1.1) over the vocabulary."""
+    w = 1.0 / torch.arange(1, vocab + 1, dtype=torch.float64) ** 1.1
+    return torch.multinomial(w / w.sum(), n, replacement=True, generator=gen).to(device)
+
+
+def _gpt_batches(n_batches, B, T, vocab, gen, device):
+    data = _zipf_tokens(n_batches * B * (T + 1), vocab, gen, "cpu").view(n_batches, B, T + 1)
+    return data[:, :, :T].contiguous().to(device), data[:, :, 1:].contiguous().to(device)
+
+
+def gpt_cpu_baseline(cfg, seconds=12.0):
+    """The reference's CPU training step (its eager ops) on a bounded batch."""
+    from oracle.eager_port import eager_indexed_gpt
+    from aiwn_b200.gpt import IndexedGPT
+    torch.set_num_threads(os.cpu_count() or 1)
+    torch.manual_seed(0)
+    m = eager_indexed_gpt(IndexedGPT(**GPT_CFG))
+    opt = torch.optim.AdamW(m.parameters(), lr=3e-4 * math.sqrt(GPT_CFG["K"] / 2), weight_decay=1e-2)
+    g = torch.Generator().manual_seed(0)
+    Bs = 4
+    x, y = _gpt_batches(1, Bs, GPT_CFG["block_size"], GPT_CFG["vocab_size"], g, "cpu")
+
+    def step():
+        opt.zero_grad()
+        _, loss = m(x[0], y[0])
+        loss.backward()
+        torch.nn.utils.clip_grad_norm_(m.parameters(), 1.0)
+        opt.step()
+
+    step()
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        step()
+        done += 1
+    dt = (time.perf_counter() - t0) / done
+    n = Bs * GPT_CFG["block_size"]
+    cores = torch.get_num_threads()
+    return {"value": n / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{done} training steps of batch {Bs} x ctx {GPT_CFG['block_size']} (the reference's eager "
+                      f"ops: IndexedLinear._eager restated in oracle/eager_port.py) in {seconds:.0f} s on {cores} threads"}
+
+
+def run_ours_gpt(args, cfg, world, rank, local):
+    """Config 5: IndexedGPT training steps, graph-replayed and eager."""
+    from aiwn_b200 import _lib
+    from aiwn_b200.gpt import GraphedTrainStep, IndexedGPT
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B, T = cfg["B"], GPT_CFG["block_size"]
+    torch.manual_seed(1234)
+    lr = 3e-4 * math.sqrt(GPT_CFG["K"] / 2)
+    gen = torch.Generator().manual_seed(99 + rank)
+    nb = 8
+    xs, ys = _gpt_batches(nb, B, T, GPT_CFG["vocab_size"], gen, dev)
+
+    def sync_all():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def time_calls(fn, reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        sync_all()
+        e0.record()
+        for k in range(reps):
+            fn(k)
+        e1.record()
+        sync_all()
+        return max_over_ranks(e0.elapsed_time(e1) / reps)
+
+    model = IndexedGPT(**GPT_CFG).to(dev)
+    if world > 1:
+        for p_ in model.parameters():
+            torch.distributed.broadcast(p_.data, 0)
+    opt = torch.optim.AdamW(model.parameters(), lr=lr, weight_decay=1e-2, capturable=True)
+    if world > 1:
+        # data-parallel: the gradient all-reduce goes inside the captured step
+        def _allreduce_hook(p_):
+            torch.distributed.all_reduce(p_.grad)
+            p_.grad.div_(world)
+        for p_ in model.parameters():
+            p_.register_post_accumulate_grad_hook(_allreduce_hook)
+    graphed = GraphedTrainStep(model, opt, B, T)
+
+    def step(k):
+        graphed(xs[k % nb], ys[k % nb])
+
+    clocks = ClockSampler(local) if rank == 0 else None
+    for k in range(max(3, args.warmup)):
+        step(k)
+    sync_all()
+    if clocks:
+        clocks.start()
+    launches0 = _lib.kernel_launches()
+    ms_step = time_calls(step, args.steps)
+    launches = _lib.kernel_launches() - launches0  # host counter: launches happened at capture
+
+    # the same step without graph replay (eager), for comparison
+    model_e = IndexedGPT(**GPT_CFG).to(dev)
+    opt_e = torch.optim.AdamW(model_e.parameters(), lr=lr, weight_decay=1e-2)
+
+    def eager_step(k):
+        opt_e.zero_grad()
+        _, loss = model_e(xs[k % nb], ys[k % nb])
+        loss.backward()
+        torch.nn.utils.clip_grad_norm_(model_e.parameters(), 1.0)
+        opt_e.step()
+
+    for k in range(3):
+        eager_step(k)
+    eager_launch0 = _lib.kernel_launches()
+    ms_eager = time_calls(eager_step, max(10, min(args.steps, 50)))
+    eager_launches = (_lib.kernel_launches() - eager_launch0) / max(10, min(args.steps, 50))
+
+    # end to end: host token batch in (pinned), loss value out
+    xh = xs.cpu().pin_memory()
+    yh = ys.cpu().pin_memory()
+    loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+
+    def e2e_step(k):
+        loss = graphed(xh[k % nb].to(dev, non_blocking=True), yh[k % nb].to(dev, non_blocking=True))
+        loss_h.copy_(loss, non_blocking=True)
+
+    ms_e2e = time_calls(e2e_step, max(10, min(args.steps, 100)))
+    clk = clocks.stop() if clocks else None
+    if rank != 0:
+        return None
+    n_tok = B * T
+    res = {
+        "metric": METRIC, "value": world * n_tok / (ms_step * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Zipf(1.1) token stream)",
+        "config": {"workload": cfg["desc"], "K": GPT_CFG["K"], "in_d": 16, "out_d": 16, "tokens_per_gpu": n_tok,
+                   "d": GPT_CFG["n_embd"], "B": B, "seq": T, "x_dtype": "f32",
+                   "parallelism": f"data-parallel dp{world}" + (" (gradient all-reduce in the graph)" if world > 1 else ""),
+                   "l2": "model and activations fit L2; steps rotate over 8 token batches"},
+        "train_step_tokens_per_s": world * n_tok / (ms_step * 1e-3),
+        "eager_step_tokens_per_s": world * n_tok / (ms_eager * 1e-3),
+        "ms": {"train_step_graph": ms_step, "train_step_eager": ms_eager},
+        "roofline": None,
+        "e2e": {"value": world * n_tok / (ms_e2e * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": 2 * n_tok * 8,
+                "d2h_bytes_per_step": 4,
+                "api": "aiwn_b200.gpt.GraphedTrainStep: host int64 token batches copied in, loss copied out"},
+        "gpu_launches": int(eager_launches * args.steps),
+        "gpu_launches_note": "library kernels per eager step x steps (graph replays launch the same kernels "
+                             "without host calls)",
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = gpt_cpu_baseline(cfg)
+    return res
+
+
 def run_ours(args, cfg, world, rank, local):
+    if cfg.get("gpt"):
+        return run_ours_gpt(args, cfg, world, rank, local)
     if cfg.get("v2"):
         return run_ours_v2(args, cfg, world, rank, local)
     from aiwn_b200 import IndexedLinear, _lib

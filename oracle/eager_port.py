@@ -55,3 +55,27 @@ def eager_step_v2(x, gamma, beta, eps, table, bias, go, bw):
     out = eager_forward(eager_cdf_norm(xl, gl, bl_, eps), tl, bl, bw)
     out.backward(go)
     return out.detach(), xl.grad, tl.grad, bl.grad
+
+
+def eager_indexed_gpt(model):
+    """Turn an ``aiwn_b200.gpt.IndexedGPT`` into the reference's CPU model: every
+    IndexedLinear runs ``_eager``'s ATen ops (``eager_forward``) and the FFN
+    takes its unfused ``up(cdf(x))`` route (GaussianCDFNorm is already the
+    reference's own two ATen ops).  For the timed CPU baseline only."""
+    import torch.nn as nn
+
+    from aiwn_b200.layers import IndexedLinear
+
+    class _EagerIL(IndexedLinear):
+        def forward(self, x):
+            shape = x.shape
+            out = eager_forward(x.reshape(-1, self.in_dim), self.table, self.bias, self.bw)
+            return out.reshape(*shape[:-1], self.out_dim)
+
+    for m in model.modules():
+        if isinstance(m, IndexedLinear):
+            m.__class__ = _EagerIL
+    for blk in model.transformer["h"]:
+        blk.ffn.up.register_forward_pre_hook(lambda mod, args: None)  # selects the unfused route
+    assert isinstance(model, nn.Module)
+    return model
