@@ -279,26 +279,41 @@ __global__ void __launch_bounds__(kSrtThreads, kSrtCtasPerSm) bwd_sorted_kernel(
     }
     if (p.want_gb) {
         // bias gradient of the j-range: the IN CTAs of a token range split it
-        // into IN parts; thread t adds chunk t % C of every (1024/C)-th row
+        // into IN parts.  Warp w sums chunk w % C of every (32 * warps per
+        // chunk)-th row from lane l's starting row, several loads in flight,
+        // then reduces over its lanes by shuffles; lane 0 adds the chunk into
+        // the CTA's sums (32/C-way contention only).
         const int q = (r1 - r0 + IN - 1) / IN;
         const int a0 = min(r1, r0 + i * q), a1 = min(r1, a0 + q);
-        constexpr int kStride = (kSrtThreads / C) * C;
-        float4 bsum = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (threadIdx.x < kStride) {
-            const int c = (int)threadIdx.x % C;
+        constexpr int kWarpsPerChunk = (kSrtThreads / 32) / C;
+        const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+        if (w < kWarpsPerChunk * C) {
+            const int c = w % C, wr = w / C;
             const float* gj = p.go + (int64_t)a0 * OUT + j0 + 4 * c;
-            const int64_t n4 = (int64_t)(a1 - a0) * C;
-            for (int64_t e = threadIdx.x; e < n4; e += kStride) {
-                const float4 v = __ldg(reinterpret_cast<const float4*>(gj + (e / C) * OUT));
+            const int nrows = a1 - a0;
+            constexpr int kStep = 32 * kWarpsPerChunk;
+            float4 bsum = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+            for (int row = wr * 32 + l; row < nrows; row += kStep) {
+                const float4 v = __ldg(reinterpret_cast<const float4*>(gj + (int64_t)row * OUT));
                 bsum.x += v.x;
                 bsum.y += v.y;
                 bsum.z += v.z;
                 bsum.w += v.w;
             }
-            atomicAdd(gbs + 4 * c + 0, bsum.x);
-            atomicAdd(gbs + 4 * c + 1, bsum.y);
-            atomicAdd(gbs + 4 * c + 2, bsum.z);
-            atomicAdd(gbs + 4 * c + 3, bsum.w);
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) {
+                bsum.x += __shfl_xor_sync(0xffffffffu, bsum.x, o);
+                bsum.y += __shfl_xor_sync(0xffffffffu, bsum.y, o);
+                bsum.z += __shfl_xor_sync(0xffffffffu, bsum.z, o);
+                bsum.w += __shfl_xor_sync(0xffffffffu, bsum.w, o);
+            }
+            if (l == 0) {
+                atomicAdd(gbs + 4 * c + 0, bsum.x);
+                atomicAdd(gbs + 4 * c + 1, bsum.y);
+                atomicAdd(gbs + 4 * c + 2, bsum.z);
+                atomicAdd(gbs + 4 * c + 3, bsum.w);
+            }
         }
         __syncthreads();
         if (a1 > a0)
