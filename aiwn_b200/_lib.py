@@ -50,6 +50,8 @@ def load():
         lib.il_workspace_bytes.restype = i64
         lib.il_backward.argtypes = [vp, vp, ci, vp, vp, vp, vp, i64, i64, i64, i64, f64, vp, i64, vp]
         lib.il_backward.restype = ci
+        lib.il_backward_accumulate.argtypes = lib.il_backward.argtypes
+        lib.il_backward_accumulate.restype = ci
         lib.il_bins.argtypes = [vp, ci, i64, i64, i64, f64, vp, vp, vp, vp]
         lib.il_bins.restype = ci
         lib.il_adam_step.argtypes = [vp, vp, vp, vp, i64, f64, f64, f64, f64, i64, vp]
@@ -144,17 +146,19 @@ def workspace_bytes(N, IN, OUT, K, x_dtype: int) -> int:
     return int(load().il_workspace_bytes(N, IN, OUT, K, x_dtype))
 
 
-def backward(go, x, table, gx, gt, gb, bw: float, workspace=None):
-    """gx / gt / gb (any may be None) <- gradients of the forward."""
+def backward(go, x, table, gx, gt, gb, bw: float, workspace=None, accumulate: bool = False):
+    """gx / gt / gb (any may be None) <- gradients of the forward; with
+    ``accumulate`` gt and gb are added into instead of overwritten."""
     _need_cuda(go, x, table, gx, gt, gb, workspace)
     N, IN = x.shape
     K, _, OUT = table.shape
     lib = load()
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    fn, name = (lib.il_backward_accumulate, "il_backward_accumulate") if accumulate else (lib.il_backward,
+                                                                                           "il_backward")
     with _on_device(x.device):
-        _check(lib.il_backward(_p(go), _p(x), x_dtype_code(x), _p(table), _p(gx), _p(gt), _p(gb),
-                               N, IN, OUT, K, float(bw), _p(workspace), ws_bytes,
-                               _stream(x.device)), "il_backward")
+        _check(fn(_p(go), _p(x), x_dtype_code(x), _p(table), _p(gx), _p(gt), _p(gb), N, IN, OUT, K, float(bw),
+                  _p(workspace), ws_bytes, _stream(x.device)), name)
 
 
 def cdf_forward(x, gamma, beta, eps: float, table, bias, xn, mean, rstd, out, bw: float):

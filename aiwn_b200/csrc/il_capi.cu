@@ -267,9 +267,11 @@ int64_t il_workspace_bytes(int64_t N, int64_t IN, int64_t OUT, int64_t K, int x_
     return il::fast_backward_workspace(N, IN, OUT, K, x_dtype);
 }
 
-int il_backward(const float* go, const void* x, int x_dtype, const float* table, void* gx,
-                float* gt, float* gb, int64_t N, int64_t IN, int64_t OUT, int64_t K, double bw,
-                void* workspace, int64_t workspace_bytes, void* stream) {
+// Every backward kernel adds into gt and gb; il_backward zeroes them first,
+// il_backward_accumulate does not.
+static int backward_impl(const float* go, const void* x, int x_dtype, const float* table, void* gx, float* gt,
+                         float* gb, int64_t N, int64_t IN, int64_t OUT, int64_t K, double bw, void* workspace,
+                         int64_t workspace_bytes, void* stream, bool accumulate) {
     int st = check_common(x, x_dtype, N, IN, K, bw);
     if (st) return st;
     if (OUT < 1) return IL_ERR_SHAPE;
@@ -281,9 +283,9 @@ int il_backward(const float* go, const void* x, int x_dtype, const float* table,
     const il::BinCfg c = make_cfg(bw, K);
     const int64_t need = il::fast_backward_workspace(N, IN, OUT, K, x_dtype);
     if (need > 0 && (!workspace || workspace_bytes < need)) return IL_ERR_WORKSPACE;
-    if (gt && cudaMemsetAsync(gt, 0, (size_t)(K * IN * OUT) * sizeof(float), s) != cudaSuccess)
+    if (!accumulate && gt && cudaMemsetAsync(gt, 0, (size_t)(K * IN * OUT) * sizeof(float), s) != cudaSuccess)
         return IL_ERR_LAUNCH;
-    if (gb && cudaMemsetAsync(gb, 0, (size_t)OUT * sizeof(float), s) != cudaSuccess)
+    if (!accumulate && gb && cudaMemsetAsync(gb, 0, (size_t)OUT * sizeof(float), s) != cudaSuccess)
         return IL_ERR_LAUNCH;
     if (N == 0) return IL_OK;
     const KernelChoice path = kernel_choice("AIWN_IL_BACKWARD", "sorted", "gather");
@@ -333,6 +335,20 @@ int il_backward(const float* go, const void* x, int x_dtype, const float* table,
         if ((st = launch_status())) return st;
     }
     return IL_OK;
+}
+
+int il_backward(const float* go, const void* x, int x_dtype, const float* table, void* gx,
+                float* gt, float* gb, int64_t N, int64_t IN, int64_t OUT, int64_t K, double bw,
+                void* workspace, int64_t workspace_bytes, void* stream) {
+    return backward_impl(go, x, x_dtype, table, gx, gt, gb, N, IN, OUT, K, bw, workspace, workspace_bytes, stream,
+                         false);
+}
+
+int il_backward_accumulate(const float* go, const void* x, int x_dtype, const float* table, void* gx,
+                           float* gt, float* gb, int64_t N, int64_t IN, int64_t OUT, int64_t K, double bw,
+                           void* workspace, int64_t workspace_bytes, void* stream) {
+    return backward_impl(go, x, x_dtype, table, gx, gt, gb, N, IN, OUT, K, bw, workspace, workspace_bytes, stream,
+                         true);
 }
 
 int il_bins(const void* x, int x_dtype, int64_t N, int64_t IN, int64_t K, double bw, int32_t* lo,

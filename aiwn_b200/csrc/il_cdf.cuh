@@ -404,7 +404,8 @@ template <int C>
 inline int launch_token_cdf(const CUtensorMap& map, const FwdArgs& a, const CdfArgs& q, const FwdPlan& pl, int sms,
                             cudaStream_t s) {
     auto kern = fwd_token_cdf_kernel<C>;
-    const int smem = pl.smem + 2 * kCdfMaxIn * 4;  // + gamma, beta
+    // slices + base alignment + one mbarrier (16 bytes) + gamma, beta
+    const int smem = a.IN * pl.slice_bytes + 128 + 16 + 2 * kCdfMaxIn * 4;
     if (smem > kSmemBudget) return kNotApplicable;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
         return 4;

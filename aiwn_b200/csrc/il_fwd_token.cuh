@@ -43,26 +43,27 @@ __global__ void __launch_bounds__(tok_threads(C), 1)
     const int IN = p.IN;
     const int j0 = blockIdx.y * p.JR;
     const uint32_t table_s = (smem_addr(smem) + 127u) & ~127u;
-    const uint32_t bar = table_s + (uint32_t)(IN * p.slice_bytes);
+    // one mbarrier per block of kTokXB input columns, so that the first pass
+    // over the tokens starts on block 0 while the later slices still load
+    const int nbar = (IN + kTokXB - 1) / kTokXB;
+    const uint32_t bar0 = table_s + (uint32_t)(IN * p.slice_bytes);
     const uint32_t row_bytes = (uint32_t)p.RS * 4;
+    const uint32_t box_bytes = (uint32_t)(p.KB * p.RS * 4);
 
     if (threadIdx.x == 0) {
         prefetch_tensormap(&tmap);
-        mbar_init(bar, 1);
+        for (int g = 0; g < nbar; ++g) mbar_init(bar0 + 8u * (uint32_t)g, 1);
         fence_mbar_init();
-        mbar_arrive_expect_tx(bar, (uint32_t)(IN * p.nbox * p.KB * p.RS * 4));
-        for (int s = 0; s < IN; ++s)
-            for (int b = 0; b < p.nbox; ++b)
-                tma_load_3d(table_s + s * p.slice_bytes + b * p.KB * p.RS * 4, &tmap, bar, j0, s, b * p.KB);
+        for (int g = 0; g < nbar; ++g) {
+            const uint32_t bar = bar0 + 8u * (uint32_t)g;
+            const int s1 = min(IN, (g + 1) * kTokXB);
+            mbar_arrive_expect_tx(bar, (uint32_t)((s1 - g * kTokXB) * p.nbox) * box_bytes);
+            for (int s = g * kTokXB; s < s1; ++s)
+                for (int b = 0; b < p.nbox; ++b)
+                    tma_load_3d(table_s + s * p.slice_bytes + b * box_bytes, &tmap, bar, j0, s, b * p.KB);
+        }
     }
-    __syncthreads();
-    mbar_wait_bounded(bar, 0);
-    for (int e = threadIdx.x; e < IN * C; e += kTokThreads) {
-        const int s = e / C, c4 = e - s * C;
-        const uint32_t sl = table_s + (uint32_t)(s * p.slice_bytes);
-        sts_v4(sl + (uint32_t)p.K * row_bytes + c4 * 16, lds_v4(sl + (uint32_t)(p.K - 1) * row_bytes + c4 * 16));
-    }
-    __syncthreads();
+    __syncthreads();  // the mbarriers are initialised
 
     const int r0 = blockIdx.x * p.ntiles;
     const int r1 = min(p.N, r0 + p.ntiles);
@@ -95,11 +96,25 @@ __global__ void __launch_bounds__(tok_threads(C), 1)
     float xpre[kTokXB];
     load_block(r0 + (int)threadIdx.x, 0, xpre);
 
+    // Every thread makes at least one pass (r0 < r1) and so waits for every
+    // block of slices before it exits.
+    bool first = true;
     for (int n = r0 + (int)threadIdx.x; n - (int)threadIdx.x < r1; n += kTokThreads) {
         float4 acc[C];
 #pragma unroll
         for (int c = 0; c < C; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int sb = 0; sb < IN; sb += kTokXB) {
+            if (first) {
+                mbar_wait_bounded(bar0 + 8u * (uint32_t)(sb / kTokXB), 0);
+                // row K of these slices = row K-1 (the top bin's hi row).  Each
+                // thread writes it before its own first read; all write the
+                // same values, and TMA never writes row K.
+                for (int s = sb; s < min(IN, sb + kTokXB); ++s) {
+                    const uint32_t sl = table_s + (uint32_t)(s * p.slice_bytes) + (uint32_t)(p.K - 1) * row_bytes;
+#pragma unroll
+                    for (int c = 0; c < C; ++c) sts_v4(sl + row_bytes + c * 16, lds_v4(sl + c * 16));
+                }
+            }
             float xv[kTokXB];
 #pragma unroll
             for (int q = 0; q < kTokXB; ++q) xv[q] = xpre[q];
@@ -127,6 +142,7 @@ __global__ void __launch_bounds__(tok_threads(C), 1)
                 }
             }
         }
+        first = false;
         if (n < r1) {
             float4* o = reinterpret_cast<float4*>(p.out + (int64_t)n * p.OUT + j0);
 #pragma unroll
@@ -159,7 +175,7 @@ inline bool plan_token_forward(int64_t N, int K, int IN, int OUT, int sms, FwdPl
         const int KB = round_up(ceil_div(K, nb), m);
         if (KB > 256) continue;
         const int slice = round_up(std::max(KB * nb, K + 1) * RS * 4, 128);
-        const int64_t smem = (int64_t)IN * slice + 128 + 16;  // + base alignment + mbarrier
+        const int64_t smem = (int64_t)IN * slice + 128 + 8 * ceil_div(IN, kTokXB);  // + alignment + mbarriers
         if (smem > kSmemBudget) continue;
         pl = {C, 1, JR, IN, KB, nb, slice, (int)smem};
         pl.RS = RS;

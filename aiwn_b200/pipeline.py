@@ -5,10 +5,11 @@ memory can be split into chunks whose host-to-device copy, forward/backward
 kernels and device-to-host copy run on three CUDA streams in a pipeline:
 while chunk c computes, chunk c+1 is being uploaded and chunk c-1's results
 are being downloaded.  Table and bias gradients add up exactly over chunks
-(they are sums over tokens), so the result equals one call on the whole
-batch up to fp32 summation order.
+(they are sums over tokens): ``il_backward_accumulate`` adds every chunk's
+into the same sums, so the result equals one call on the whole batch up to
+fp32 summation order.
 
-    step = HostPipeline(layer, chunks=4)
+    step = HostPipeline(layer)          # chunk count tuned per batch shape on first use
     step.forward_backward(x_host, go_host, out_host, gx_host)   # pinned tensors
 
 The whole multi-stream step (copies, kernels, per-chunk gradient sums) is
@@ -19,6 +20,8 @@ same as for device tensors.
 """
 from __future__ import annotations
 
+import time
+
 import torch
 
 from . import _lib
@@ -26,32 +29,48 @@ from . import _lib
 
 class HostPipeline:
     """Chunked, stream-overlapped forward(+backward) of an IndexedLinear (or
-    TokenParallelIndexedLinear) over pinned host tensors."""
+    TokenParallelIndexedLinear) over pinned host tensors.
 
-    def __init__(self, layer, chunks: int = 4, device=None, graphs: bool = True):
+    Each chunk gets its own device buffers (x, go, out, dx) as long as the
+    whole batch fits ``max_resident_bytes``; then the only ordering between
+    chunks is that of each stream, and the upload of chunk c+1 never waits for
+    chunk c's results to leave.  Larger batches reuse a ring of slots.
+    """
+
+    # chunk counts tried when none is given
+    TUNE_CHUNKS = (1, 2, 4, 8, 16)
+    TUNE_MIN_CHUNK = 4096  # tokens
+
+    def __init__(self, layer, chunks: int | None = None, device=None, graphs: bool = True,
+                 max_resident_bytes: int = 1 << 30):
         self.layer = layer
         inner = getattr(layer, "layer", layer)
         self.inner = inner
-        self.chunks = max(1, int(chunks))
+        self.auto = chunks is None
+        self.chunks = 1 if chunks is None else max(1, int(chunks))
+        self._tuned = {}  # (N, in, out, x dtype) -> tuned HostPipeline
         self.device = torch.device(device) if device is not None else inner.table.device
         self.s_h2d = torch.cuda.Stream(self.device)
         self.s_cmp = torch.cuda.Stream(self.device)
         self.s_d2h = torch.cuda.Stream(self.device)
         self.graphs = graphs
+        self.max_resident_bytes = int(max_resident_bytes)
         self._bufs = None
         self._ws = None
         self._graph_cache = {}
 
     def _buffers(self, n, IN, OUT, xdtype):
-        key = (n, IN, OUT, xdtype)
+        key = (n, IN, OUT, xdtype, self.chunks)
         if self._bufs is None or self._bufs[0] != key:
             mk = lambda *s, dt=torch.float32: torch.empty(*s, dtype=dt, device=self.device)  # noqa: E731
-            # two slots per stream stage so chunk c+1 can land while chunk c computes
+            xs = torch.empty(0, dtype=xdtype).element_size()
+            slot_bytes = n * (2 * IN * xs + 2 * OUT * 4)
+            nslots = max(2, min(self.chunks, self.max_resident_bytes // max(slot_bytes, 1)))
             slots = [dict(x=mk(n, IN, dt=xdtype), go=mk(n, OUT), out=mk(n, OUT), gx=mk(n, IN, dt=xdtype))
-                     for _ in range(2)]
+                     for _ in range(nslots)]
             K = self.inner.K
-            # per-chunk gradients and their running sums over the chunks
-            grads = dict(gt=mk(K, IN, OUT), gb=mk(OUT), gt_sum=mk(K, IN, OUT), gb_sum=mk(OUT))
+            # the gradients of all chunks add up here (il_backward_accumulate)
+            grads = dict(gt_sum=mk(K, IN, OUT), gb_sum=mk(OUT))
             self._bufs = (key, slots, grads)
             self._graph_cache.clear()
         return self._bufs[1], self._bufs[2]
@@ -64,6 +83,7 @@ class HostPipeline:
         OUT, K = inner.out_dim, inner.K
         n = (N + self.chunks - 1) // self.chunks
         slots, gr = self._buffers(n, IN, OUT, x_host.dtype)
+        S = len(slots)
         ws_n = _lib.workspace_bytes(n, IN, OUT, K, _lib.x_dtype_code(slots[0]["x"]))
         if ws_n and (self._ws is None or self._ws.numel() < ws_n):
             self._ws = torch.empty(ws_n, dtype=torch.uint8, device=self.device)
@@ -74,41 +94,69 @@ class HostPipeline:
         # parameters (and the sums just zeroed) were written on the caller's stream
         for s in (self.s_h2d, self.s_cmp, self.s_d2h):
             s.wait_stream(cur)
-        up_done = [torch.cuda.Event() for _ in range(2)]
-        cmp_done = [torch.cuda.Event() for _ in range(2)]
-        down_done = [torch.cuda.Event() for _ in range(2)]
+        ev = lambda: torch.cuda.Event()  # noqa: E731
+        x_up, go_up, fwd_done, bwd_done, out_down, gx_down = [], [], [], [], [], []
         for c in range(self.chunks):
             a, b = c * n, min(N, (c + 1) * n)
             if a >= b:
                 break
             m = b - a
-            sl = slots[c & 1]
+            sl = slots[c % S]
+            for lst in (x_up, go_up, fwd_done, bwd_done, out_down, gx_down):
+                lst.append(ev())
             with torch.cuda.stream(self.s_h2d):
-                if c >= 2:
-                    self.s_h2d.wait_event(cmp_done[c & 1])  # slot's inputs consumed
+                if c >= S:
+                    self.s_h2d.wait_event(bwd_done[c - S])  # the slot's inputs are consumed
                 sl["x"][:m].copy_(x_host[a:b], non_blocking=True)
+                x_up[c].record(self.s_h2d)
                 sl["go"][:m].copy_(go_host[a:b], non_blocking=True)
-                up_done[c & 1].record(self.s_h2d)
+                go_up[c].record(self.s_h2d)
             with torch.cuda.stream(self.s_cmp):
-                self.s_cmp.wait_event(up_done[c & 1])
-                if c >= 2:
-                    self.s_cmp.wait_event(down_done[c & 1])  # slot's outputs downloaded
                 xs, gos = sl["x"][:m], sl["go"][:m]
+                self.s_cmp.wait_event(x_up[c])
+                if c >= S:
+                    self.s_cmp.wait_event(out_down[c - S])  # the slot's out has left
                 _lib.forward(xs, table, bias, sl["out"][:m], inner.bw)
-                _lib.backward(gos, xs, table, sl["gx"][:m], gr["gt"] if want_grads else None,
-                              gr["gb"] if want_grads else None, inner.bw, self._ws if ws_n else None)
-                if want_grads:
-                    gr["gt_sum"].add_(gr["gt"])
-                    gr["gb_sum"].add_(gr["gb"])
-                cmp_done[c & 1].record(self.s_cmp)
+                fwd_done[c].record(self.s_cmp)
+                self.s_cmp.wait_event(go_up[c])
+                if c >= S:
+                    self.s_cmp.wait_event(gx_down[c - S])
+                _lib.backward(gos, xs, table, sl["gx"][:m], gr["gt_sum"] if want_grads else None,
+                              gr["gb_sum"] if want_grads else None, inner.bw, self._ws if ws_n else None,
+                              accumulate=True)
+                bwd_done[c].record(self.s_cmp)
             with torch.cuda.stream(self.s_d2h):
-                self.s_d2h.wait_event(cmp_done[c & 1])
+                self.s_d2h.wait_event(fwd_done[c])
                 out_host[a:b].copy_(sl["out"][:m], non_blocking=True)
+                out_down[c].record(self.s_d2h)
+                self.s_d2h.wait_event(bwd_done[c])
                 gx_host[a:b].copy_(sl["gx"][:m], non_blocking=True)
-                down_done[c & 1].record(self.s_d2h)
+                gx_down[c].record(self.s_d2h)
         for s in (self.s_h2d, self.s_cmp, self.s_d2h):
             cur.wait_stream(s)
         return gr
+
+    def _tune(self, x_host, go_host, out_host, gx_host):
+        """The fastest chunk count for this batch shape on this host: host
+        to device copies are slower for small pieces on some hosts while
+        every chunk adds the kernels' fixed cost, so the best split depends
+        on the machine.  Each candidate runs one untimed and three timed
+        steps (gradients stay in the pipeline's own sums)."""
+        N = x_host.shape[0]
+        cands = [c for c in self.TUNE_CHUNKS if c == 1 or N // c >= self.TUNE_MIN_CHUNK]
+        best = None
+        for c in cands:
+            p = HostPipeline(self.layer, chunks=c, device=self.device, graphs=self.graphs,
+                             max_resident_bytes=self.max_resident_bytes)
+            p._run(x_host, go_host, out_host, gx_host, True)
+            t0 = time.perf_counter()
+            for _ in range(3):
+                p._run(x_host, go_host, out_host, gx_host, True)
+            dt = time.perf_counter() - t0
+            if best is None or dt < best[0]:
+                best = (dt, p)
+            del p
+        return best[1]
 
     def forward_backward(self, x_host, go_host, out_host, gx_host, accumulate_grads: bool = True):
         """out_host <- layer(x_host); gx_host <- d/dx; table.grad/bias.grad +=.
@@ -118,33 +166,54 @@ class HostPipeline:
         for t in (x_host, go_host, out_host, gx_host):
             if not t.is_pinned():
                 raise ValueError("HostPipeline needs pinned host tensors (tensor.pin_memory())")
+        runner = self
+        if self.auto:
+            key = (tuple(x_host.shape), tuple(go_host.shape), x_host.dtype)
+            runner = self._tuned.get(key)
+            if runner is None:
+                runner = self._tune(x_host, go_host, out_host, gx_host)
+                self._tuned[key] = runner
+        gr = runner._run(x_host, go_host, out_host, gx_host, accumulate_grads)
+        if accumulate_grads:
+            for p, s in ((self.inner.table, gr["gt_sum"]), (self.inner.bias, gr["gb_sum"])):
+                if p.grad is None:
+                    p.grad = s.clone()
+                else:
+                    p.grad.add_(s)
+        torch.cuda.current_stream(self.device).synchronize()
+        return out_host, gx_host
+
+    @property
+    def chosen_chunks(self) -> dict:
+        """Chunk count in use per batch size N (the tuned ones when auto)."""
+        if not self.auto:
+            return {"all": self.chunks}
+        return {k[0][0]: p.chunks for k, p in self._tuned.items()}
+
+    def _run(self, x_host, go_host, out_host, gx_host, want_grads: bool):
+        """One pipelined step with this instance's chunk count; returns the
+        gradient sums (valid once the current stream reaches this point)."""
         inner = self.inner
         table, bias = inner.table.detach(), inner.bias.detach()
         cur = torch.cuda.current_stream(self.device)
         if self.graphs:
             key = (x_host.data_ptr(), go_host.data_ptr(), out_host.data_ptr(), gx_host.data_ptr(),
-                   tuple(x_host.shape), x_host.dtype, table.data_ptr(), bias.data_ptr(), bool(accumulate_grads))
+                   tuple(x_host.shape), x_host.dtype, table.data_ptr(), bias.data_ptr(), bool(want_grads))
             entry = self._graph_cache.get(key)
             if entry is None:
                 # one eager step first: the library's per-device setup and the
                 # kernels' attributes are then in place before capture
-                gr = self._issue(x_host, go_host, out_host, gx_host, table, bias, accumulate_grads)
+                gr = self._issue(x_host, go_host, out_host, gx_host, table, bias, want_grads)
                 cur.synchronize()
                 g = torch.cuda.CUDAGraph()
                 # captured on torch's side capture stream; replayed on `cur`
                 with torch.cuda.graph(g, capture_error_mode="relaxed"):
-                    gr = self._issue(x_host, go_host, out_host, gx_host, table, bias, accumulate_grads)
+                    gr = self._issue(x_host, go_host, out_host, gx_host, table, bias, want_grads)
                 entry = (g, gr)
                 self._graph_cache[key] = entry
             entry[0].replay()
             gr = entry[1]
         else:
-            gr = self._issue(x_host, go_host, out_host, gx_host, table, bias, accumulate_grads)
-        if accumulate_grads:
-            for p, s in ((inner.table, gr["gt_sum"]), (inner.bias, gr["gb_sum"])):
-                if p.grad is None:
-                    p.grad = s.clone()
-                else:
-                    p.grad.add_(s)
+            gr = self._issue(x_host, go_host, out_host, gx_host, table, bias, want_grads)
         cur.synchronize()
-        return out_host, gx_host
+        return gr

@@ -673,9 +673,8 @@ def run_ours(args, cfg, world, rank, local):
     goh = [g.cpu().pin_memory() for g in gos[:2]]
     outh = [torch.empty(N, OUT).pin_memory() for _ in range(2)]
     gxh = [torch.empty(N, IN, dtype=xs[0].dtype).pin_memory() for _ in range(2)]
-    # chunking pays off once a chunk is large enough to keep the copy engines busy
-    e2e_chunks = max(1, min(8, N // 16384))
-    pipe = HostPipeline(m, chunks=e2e_chunks)
+    # chunk count tuned by the pipeline on its first call (the untimed warm-up)
+    pipe = HostPipeline(m)
 
     def e2e_step(k):
         i = k % 2
@@ -728,8 +727,9 @@ def run_ours(args, cfg, world, rank, local):
                 "h2d_bytes_per_step": xh[0].numel() * xh[0].element_size() + goh[0].numel() * 4,
                 "d2h_bytes_per_step": N * OUT * 4 + gxh[0].numel() * gxh[0].element_size(),
                 "api": "aiwn_b200.pipeline.HostPipeline over TokenParallelIndexedLinear: forward+backward "
-                       f"of pinned host x/go into pinned host out/dx, {e2e_chunks} chunks with copies "
-                       "overlapped, replayed as one CUDA graph (+gradient all-reduce when N>1)"},
+                       f"of pinned host x/go into pinned host out/dx, {pipe.chosen_chunks.get(N)} chunks "
+                       "(tuned on the first call) with copies overlapped, replayed as one CUDA graph "
+                       "(+gradient all-reduce when N>1)"},
         "gpu_launches": launches,
         "clocks": clk,
     }

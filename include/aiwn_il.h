@@ -102,6 +102,18 @@ IL_API int il_backward(const float* go, const void* x, int x_dtype, const float*
                 void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
+ * il_backward with gt and gb added into instead of overwritten: the caller
+ * zeroes them once, then one call per chunk of a batch sums the chunks'
+ * gradients in place (gx is still written, not accumulated).  The reference
+ * has no counterpart (autograd returns fresh gradients); it serves chunked
+ * passes over a batch, such as the host-buffer pipeline, without an extra
+ * add per chunk.
+ */
+IL_API int il_backward_accumulate(const float* go, const void* x, int x_dtype, const float* table, void* gx,
+                           float* gt, float* gb, int64_t N, int64_t IN, int64_t OUT, int64_t K, double bw,
+                           void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
  * Bins of every x element: lo (int32), hi (int32), fr (fp32); any output may
  * be NULL.  Bit-exact with aiwn/layers/indexed_linear.py:175-177.
  */

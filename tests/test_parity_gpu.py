@@ -185,11 +185,34 @@ def test_device_status_clean():
     _lib.check_device_status()
 
 
+def test_backward_accumulate_adds_into_grads():
+    """il_backward_accumulate: gt / gb grow by the gradients of each call
+    (chunks of a batch sum to the whole batch's); dx is written per call."""
+    c = CASES[2]
+    x, table, bias, go = make_inputs(c)
+    bw = 2.0 / c.K
+    out, gx, gt, gb = run_ours(x, table, bias, go, bw)
+    x, table, go = x.to(DEV), table.to(DEV), go.to(DEV)
+    h = x.shape[0] // 3
+    gt_acc = torch.full_like(gt, 0.5)
+    gb_acc = torch.full_like(gb, -0.25)
+    gx_acc = torch.empty_like(gx)
+    for a, b in ((0, h), (h, x.shape[0])):
+        _lib.backward(go[a:b], x[a:b], table, gx_acc[a:b], gt_acc, gb_acc, bw, accumulate=True)
+    torch.cuda.synchronize()
+    normwise_close(gt_acc.cpu().numpy() - 0.5, gt.cpu().numpy(), GRAD_RTOL, "accumulated gt")
+    normwise_close(gb_acc.cpu().numpy() + 0.25, gb.cpu().numpy(), GRAD_RTOL, "accumulated gb")
+    normwise_close(gx_acc.cpu().numpy(), gx.cpu().numpy(), 1e-6, "dx of the chunks")
+
+
+@pytest.mark.parametrize("chunks,resident", [(5, True), (5, False), (None, True)],
+                         ids=["per_chunk_buffers", "slot_ring", "tuned_chunks"])
 @pytest.mark.parametrize("graphs", [True, False])
-def test_host_pipeline_matches_whole_batch_call(graphs):
+def test_host_pipeline_matches_whole_batch_call(graphs, chunks, resident):
     """HostPipeline (chunked, copies overlapped on three streams, replayed
-    from a CUDA graph or issued eagerly) gives the same out / dx as one call
-    on the whole batch and the same summed grads."""
+    from a CUDA graph or issued eagerly; device buffers per chunk or a ring
+    of two reused slots) gives the same out / dx as one call on the whole
+    batch and the same summed grads."""
     from aiwn_b200.pipeline import HostPipeline
     c = CASES[2]
     x, table, bias, go = make_inputs(c)
@@ -202,7 +225,7 @@ def test_host_pipeline_matches_whole_batch_call(graphs):
     xh, goh = x.pin_memory(), go.pin_memory()
     outh = torch.empty(N, c.OUT).pin_memory()
     gxh = torch.empty(N, c.IN).pin_memory()
-    pipe = HostPipeline(m, chunks=5, graphs=graphs)
+    pipe = HostPipeline(m, chunks=chunks, graphs=graphs, max_resident_bytes=(1 << 30) if resident else 1)
     for _ in range(2):  # second call reuses the buffers (and the graph); grads accumulate
         pipe.forward_backward(xh, goh, outh, gxh)
     torch.cuda.synchronize()
@@ -211,3 +234,5 @@ def test_host_pipeline_matches_whole_batch_call(graphs):
     normwise_close(gxh.numpy(), gx.cpu().numpy(), 1e-6, "pipeline gx")
     normwise_close(m.table.grad.cpu().numpy(), 2 * gt.cpu().numpy(), GRAD_RTOL, "pipeline gt")
     normwise_close(m.bias.grad.cpu().numpy(), 2 * gb.cpu().numpy(), GRAD_RTOL, "pipeline gb")
+    if chunks is None:
+        assert pipe.chosen_chunks[N] in HostPipeline.TUNE_CHUNKS
