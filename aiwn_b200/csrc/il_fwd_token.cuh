@@ -26,7 +26,8 @@
 
 namespace il {
 
-constexpr int kTokXB = 4;  // input columns per x block (prefetched one block ahead)
+constexpr int kTokXB = 4;     // input columns per x block (prefetched one block ahead)
+constexpr int kTokAhead = 2;  // blocks of table slices in flight during the first pass
 
 // threads per CTA (one token each): more warps hide latency where the
 // per-token state is small
@@ -43,25 +44,28 @@ __global__ void __launch_bounds__(tok_threads(C), 1)
     const int IN = p.IN;
     const int j0 = blockIdx.y * p.JR;
     const uint32_t table_s = (smem_addr(smem) + 127u) & ~127u;
-    // one mbarrier per block of kTokXB input columns, so that the first pass
-    // over the tokens starts on block 0 while the later slices still load
+    // One mbarrier per block of kTokXB input columns.  Thread 0 keeps
+    // kTokAhead blocks in flight and issues block g + kTokAhead once block g
+    // has landed, so that the blocks arrive one after another and the first
+    // pass over the tokens works on block g while the next ones load.
     const int nbar = (IN + kTokXB - 1) / kTokXB;
     const uint32_t bar0 = table_s + (uint32_t)(IN * p.slice_bytes);
     const uint32_t row_bytes = (uint32_t)p.RS * 4;
     const uint32_t box_bytes = (uint32_t)(p.KB * p.RS * 4);
+    auto issue_block = [&](int g) {
+        const uint32_t bar = bar0 + 8u * (uint32_t)g;
+        const int s1 = min(IN, (g + 1) * kTokXB);
+        mbar_arrive_expect_tx(bar, (uint32_t)((s1 - g * kTokXB) * p.nbox) * box_bytes);
+        for (int s = g * kTokXB; s < s1; ++s)
+            for (int b = 0; b < p.nbox; ++b)
+                tma_load_3d(table_s + s * p.slice_bytes + b * box_bytes, &tmap, bar, j0, s, b * p.KB);
+    };
 
     if (threadIdx.x == 0) {
         prefetch_tensormap(&tmap);
         for (int g = 0; g < nbar; ++g) mbar_init(bar0 + 8u * (uint32_t)g, 1);
         fence_mbar_init();
-        for (int g = 0; g < nbar; ++g) {
-            const uint32_t bar = bar0 + 8u * (uint32_t)g;
-            const int s1 = min(IN, (g + 1) * kTokXB);
-            mbar_arrive_expect_tx(bar, (uint32_t)((s1 - g * kTokXB) * p.nbox) * box_bytes);
-            for (int s = g * kTokXB; s < s1; ++s)
-                for (int b = 0; b < p.nbox; ++b)
-                    tma_load_3d(table_s + s * p.slice_bytes + b * box_bytes, &tmap, bar, j0, s, b * p.KB);
-        }
+        for (int g = 0; g < min(nbar, kTokAhead); ++g) issue_block(g);
     }
     __syncthreads();  // the mbarriers are initialised
 
@@ -96,8 +100,8 @@ __global__ void __launch_bounds__(tok_threads(C), 1)
     float xpre[kTokXB];
     load_block(r0 + (int)threadIdx.x, 0, xpre);
 
-    // Every thread makes at least one pass (r0 < r1) and so waits for every
-    // block of slices before it exits.
+    // Every thread makes at least one pass (r0 < r1), so it waits for every
+    // block of slices before it exits, and thread 0 issues every block.
     bool first = true;
     for (int n = r0 + (int)threadIdx.x; n - (int)threadIdx.x < r1; n += kTokThreads) {
         float4 acc[C];
@@ -105,7 +109,9 @@ __global__ void __launch_bounds__(tok_threads(C), 1)
         for (int c = 0; c < C; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int sb = 0; sb < IN; sb += kTokXB) {
             if (first) {
-                mbar_wait_bounded(bar0 + 8u * (uint32_t)(sb / kTokXB), 0);
+                const int g = sb / kTokXB;
+                mbar_wait_bounded(bar0 + 8u * (uint32_t)g, 0);
+                if (threadIdx.x == 0 && g + kTokAhead < nbar) issue_block(g + kTokAhead);
                 // row K of these slices = row K-1 (the top bin's hi row).  Each
                 // thread writes it before its own first read; all write the
                 // same values, and TMA never writes row K.
