@@ -78,38 +78,43 @@ __global__ void __launch_bounds__(kCdfThreads, 1)
     const int IN = p.IN;
     const int j0 = blockIdx.y * p.JR;
     const uint32_t table_s = (smem_addr(smem) + 127u) & ~127u;
-    const uint32_t bar = table_s + (uint32_t)(IN * p.slice_bytes);
+    // the slices load as in fwd_token_kernel: blocks of kTokXB columns, one
+    // mbarrier each, kTokAhead blocks in flight, waited for in the first pass
+    const int nbar = (IN + kTokXB - 1) / kTokXB;
+    const uint32_t bar0 = table_s + (uint32_t)(IN * p.slice_bytes);
     const uint32_t row_bytes = (uint32_t)p.RS * 4;
+    const uint32_t box_bytes = (uint32_t)(p.KB * p.RS * 4);
+    auto issue_block = [&](int g) {
+        const uint32_t bar = bar0 + 8u * (uint32_t)g;
+        const int s1 = min(IN, (g + 1) * kTokXB);
+        mbar_arrive_expect_tx(bar, (uint32_t)((s1 - g * kTokXB) * p.nbox) * box_bytes);
+        for (int s = g * kTokXB; s < s1; ++s)
+            for (int b = 0; b < p.nbox; ++b)
+                tma_load_3d(table_s + s * p.slice_bytes + b * box_bytes, &tmap, bar, j0, s, b * p.KB);
+    };
 
     if (threadIdx.x == 0) {
         prefetch_tensormap(&tmap);
-        mbar_init(bar, 1);
+        for (int g = 0; g < nbar; ++g) mbar_init(bar0 + 8u * (uint32_t)g, 1);
         fence_mbar_init();
-        mbar_arrive_expect_tx(bar, (uint32_t)(IN * p.nbox * p.KB * p.RS * 4));
-        for (int s = 0; s < IN; ++s)
-            for (int b = 0; b < p.nbox; ++b)
-                tma_load_3d(table_s + s * p.slice_bytes + b * p.KB * p.RS * 4, &tmap, bar, j0, s, b * p.KB);
+        for (int g = 0; g < min(nbar, kTokAhead); ++g) issue_block(g);
     }
-    __syncthreads();
-    mbar_wait_bounded(bar, 0);
-    for (int e = threadIdx.x; e < IN * C; e += kCdfThreads) {
-        const int s = e / C, c4 = e - s * C;
-        const uint32_t sl = table_s + (uint32_t)(s * p.slice_bytes);
-        sts_v4(sl + (uint32_t)p.K * row_bytes + c4 * 16, lds_v4(sl + (uint32_t)(p.K - 1) * row_bytes + c4 * 16));
-    }
-    __syncthreads();
 
     const int r0 = blockIdx.x * p.ntiles;  // this CTA's token range (ntiles = its length)
     const int r1 = min(p.N, r0 + p.ntiles);
     const float* x = reinterpret_cast<const float*>(p.x);
     const bool writer = blockIdx.y == 0;
-    // gamma, beta staged after the mbarrier (bytes [bar + 16, bar + 16 + 8*IN))
-    float* gb_s = reinterpret_cast<float*>(smem + (bar + 16 - smem_addr(smem)));
+    // gamma, beta staged after the mbarriers (bytes [gb, gb + 8*kCdfMaxIn))
+    const uint32_t gb_addr = bar0 + 8u * (uint32_t)nbar;
+    float* gb_s = reinterpret_cast<float*>(smem + (gb_addr - smem_addr(smem)));
     for (int k = threadIdx.x; k < IN; k += kCdfThreads) {
         gb_s[k] = q.gamma[k];
         gb_s[kCdfMaxIn + k] = q.beta[k];
     }
-    __syncthreads();
+    __syncthreads();  // gamma, beta staged; the mbarriers are initialised
+    // Every thread makes at least one pass (r0 < r1), so it waits for every
+    // block of slices before it exits, and thread 0 issues every block.
+    bool first = true;
     for (int n = r0 + (int)threadIdx.x; n - (int)threadIdx.x < r1; n += kCdfThreads) {
         const bool ok = n < r1;
         float v[kCdfMaxIn];
@@ -155,6 +160,18 @@ __global__ void __launch_bounds__(kCdfThreads, 1)
 #pragma unroll
         for (int s = 0; s < kCdfMaxIn; ++s) {
             if (s >= IN) break;
+            if (first && s % kTokXB == 0) {
+                const int g = s / kTokXB;
+                mbar_wait_bounded(bar0 + 8u * (uint32_t)g, 0);
+                if (threadIdx.x == 0 && g + kTokAhead < nbar) issue_block(g + kTokAhead);
+                // row K = row K-1 (the top bin's hi row), written by every
+                // thread before its own first read; TMA never writes row K
+                for (int t = s; t < min(IN, s + kTokXB); ++t) {
+                    const uint32_t sl = table_s + (uint32_t)(t * p.slice_bytes) + (uint32_t)(p.K - 1) * row_bytes;
+#pragma unroll
+                    for (int c = 0; c < C; ++c) sts_v4(sl + row_bytes + c * 16, lds_v4(sl + c * 16));
+                }
+            }
             int lo;
             float wa, wc;
             gather_weights<kF32>(v[s], p.cfg, lo, wa, wc);
@@ -173,6 +190,7 @@ __global__ void __launch_bounds__(kCdfThreads, 1)
                 acc[c].w = fmaf(wc, th.w, acc[c].w);
             }
         }
+        first = false;
         if (ok) {
             float4* o = reinterpret_cast<float4*>(p.out + (int64_t)n * p.OUT + j0);
 #pragma unroll
@@ -404,8 +422,8 @@ template <int C>
 inline int launch_token_cdf(const CUtensorMap& map, const FwdArgs& a, const CdfArgs& q, const FwdPlan& pl, int sms,
                             cudaStream_t s) {
     auto kern = fwd_token_cdf_kernel<C>;
-    // slices + base alignment + one mbarrier (16 bytes) + gamma, beta
-    const int smem = a.IN * pl.slice_bytes + 128 + 16 + 2 * kCdfMaxIn * 4;
+    // slices + base alignment + mbarriers + gamma, beta
+    const int smem = a.IN * pl.slice_bytes + 128 + 8 * ceil_div(a.IN, kTokXB) + 2 * kCdfMaxIn * 4;
     if (smem > kSmemBudget) return kNotApplicable;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
         return 4;
