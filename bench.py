@@ -218,6 +218,45 @@ def run_reference(args, cfg, world, rank):
     }
 
 
+REF_CUDA_SO = os.path.join(ROOT, "baseline", "_ref", "indexed_linear_cuda.so")
+
+
+def reference_gpu(cfg, x, table, bias, go, reps=3):
+    """The reference's own CUDA extension (aiwn/layers/indexed_linear_cuda.cu,
+    built for sm_100a by baseline/build_ref_cuda.py) timed on the same
+    device-resident inputs: its forward, and its backward (dx and dtable; it
+    has no dbias).  Reported beside the result, not as it.  Its kernels take
+    fp32 x in [-1, 1] only (the low bin is not clamped), so other inputs are
+    not run."""
+    if cfg["dtype"] != "f32" or cfg["xdist"] != "uniform":
+        return {"unavailable": "the reference's CUDA extension takes fp32 x in [-1, 1] only"}
+    if not os.path.exists(REF_CUDA_SO):
+        return {"unavailable": "not built here (python baseline/build_ref_cuda.py)"}
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("indexed_linear_cuda", REF_CUDA_SO)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    bw = 2.0 / cfg["K"]
+
+    def timed(fn):
+        fn()  # warm-up
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()  # the extension launches on the legacy default stream, torch's current one here
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    ms_f = timed(lambda: mod.forward(x, table, bias, bw))
+    ms_b = timed(lambda: mod.backward(go, x, table, bw))
+    n = x.shape[0]
+    return {"source": "aiwn/layers/indexed_linear_cuda.cu, built for sm_100a", "fwd_ms": ms_f, "bwd_ms": ms_b,
+            "fwd_tokens_per_s": n / (ms_f * 1e-3), "fwd_bwd_tokens_per_s": n / ((ms_f + ms_b) * 1e-3),
+            "reps": reps, "inputs": "the bench's first x/go set, device-resident"}
+
+
 def cpu_baseline(cfg, seconds=12.0):
     """The reference's CPU path on a bounded sample of the workload."""
     torch.set_num_threads(os.cpu_count() or 1)
@@ -733,6 +772,8 @@ def run_ours(args, cfg, world, rank, local):
         "gpu_launches": launches,
         "clocks": clk,
     }
+    if world == 1 and not args.no_reference_gpu:
+        res["reference_gpu"] = reference_gpu(cfg, xs[0], table, bias, gos[0])
     if world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(cfg)
     return res
@@ -746,6 +787,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c3")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own CUDA extension (when built)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
     world, rank, local = dist_setup(args)
