@@ -56,12 +56,15 @@ def check_against_oracle(c, x, table, bias, go):
     assert same_bits(fr.cpu().numpy(), rfr)
 
 
-@pytest.mark.parametrize("paths", [("auto", "auto"), ("cluster", "gather")], ids=["auto", "alt"])
+@pytest.mark.parametrize("paths", [("auto", "auto"), ("token", "sorted"), ("cluster", "gather")],
+                         ids=["auto", "pinned", "alt"])
 @pytest.mark.parametrize("c", CASES + EDGE_CASES, ids=lambda c: c.name)
 def test_parity_vs_oracle(c, paths, monkeypatch):
-    """auto: one token per lane forward and bin-sorted backward wherever they
-    have a plan; alt: the cluster forward and the gather backward with
-    per-token table-gradient reductions."""
+    """auto: the library's own choice (cluster forward for rows of >= 32
+    outputs, else one token per lane; bin-sorted backward) wherever there is a
+    plan; pinned: the token forward and the sorted backward wherever they have
+    a plan; alt: the cluster forward and the gather backward with per-token
+    table-gradient reductions."""
     monkeypatch.setenv("AIWN_IL_FORWARD", paths[0])
     monkeypatch.setenv("AIWN_IL_BACKWARD", paths[1])
     x, table, bias, go = make_inputs(c)
