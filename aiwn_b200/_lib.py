@@ -60,6 +60,10 @@ def load():
         lib.il_cdf_forward.restype = ci
         lib.il_cdf_backward.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
         lib.il_cdf_backward.restype = ci
+        lib.il_layernorm_forward.argtypes = [vp, vp, vp, f64, vp, vp, vp, i64, i64, vp]
+        lib.il_layernorm_forward.restype = ci
+        lib.il_layernorm_backward.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+        lib.il_layernorm_backward.restype = ci
         lib.il_bin_counts.argtypes = [vp, ci, i64, i64, i64, f64, vp, vp]
         lib.il_bin_counts.restype = ci
         lib.il_kernel_launches.argtypes = []
@@ -185,6 +189,28 @@ def cdf_backward(gxn, x, gamma, beta, mean, rstd, dx, dgamma, dbeta):
     with _on_device(x.device):
         _check(lib.il_cdf_backward(_p(gxn), _p(x), _p(gamma), _p(beta), _p(mean), _p(rstd), _p(dx), _p(dgamma),
                                    _p(dbeta), N, IN, _stream(x.device)), "il_cdf_backward")
+
+
+def layernorm_forward(x, gamma, beta, eps: float, y, mean, rstd):
+    """y <- LayerNorm(x; gamma, beta, eps) over the last dim (fp32 x [N, IN],
+    IN <= 32); also the per-row mean and rstd [N]."""
+    _need_cuda(x, gamma, beta, y, mean, rstd)
+    N, IN = x.shape
+    lib = load()
+    with _on_device(x.device):
+        _check(lib.il_layernorm_forward(_p(x), _p(gamma), _p(beta), float(eps), _p(y), _p(mean), _p(rstd), N, IN,
+                                        _stream(x.device)), "il_layernorm_forward")
+    return y
+
+
+def layernorm_backward(gy, x, gamma, mean, rstd, dx, dgamma, dbeta):
+    """dx / dgamma / dbeta (any may be None) <- backward of layernorm_forward."""
+    _need_cuda(gy, x, gamma, mean, rstd, dx, dgamma, dbeta)
+    N, IN = x.shape
+    lib = load()
+    with _on_device(x.device):
+        _check(lib.il_layernorm_backward(_p(gy), _p(x), _p(gamma), _p(mean), _p(rstd), _p(dx), _p(dgamma),
+                                         _p(dbeta), N, IN, _stream(x.device)), "il_layernorm_backward")
 
 
 def bin_counts(x, K: int, bw: float, counts):

@@ -284,6 +284,59 @@ int il_cdf_backward(const float* gxn, const float* x, const float* gamma, const 
     return launch_status();
 }
 
+int il_layernorm_forward(const float* x, const float* gamma, const float* beta, double eps, float* y, float* mean,
+                         float* rstd, int64_t N, int64_t IN, void* stream) {
+    if (N < 0 || IN < 1 || IN > il::kCdfMaxIn || N > INT32_MAX) return IL_ERR_SHAPE;
+    if (!(eps >= 0.0)) return IL_ERR_VALUE;
+    if (N == 0) return IL_OK;
+    if (!x || !gamma || !beta || !y || !mean || !rstd) return IL_ERR_NULL;
+    int sms = 0;
+    int st = check_device(&sms);
+    if (st) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    il::CdfArgs q;
+    q.gamma = gamma;
+    q.beta = beta;
+    q.eps = (float)eps;
+    q.xn = y;
+    q.mean = mean;
+    q.rstd = rstd;
+    const unsigned blocks = (unsigned)((N + il::kCdfRowThreads - 1) / il::kCdfRowThreads);
+    const int vec = (IN % 4 == 0) && ((((uintptr_t)x | (uintptr_t)y) & 15) == 0);
+    auto run = [&](auto kern) { kern<<<blocks, il::kCdfRowThreads, 0, s>>>(x, q, (int)N, (int)IN, vec); };
+    if (IN <= 8) run(il::cdf_prologue_small_kernel<8, false>);
+    else if (IN <= 16) run(il::cdf_prologue_small_kernel<16, false>);
+    else if (IN <= 24) run(il::cdf_prologue_small_kernel<24, false>);
+    else run(il::cdf_prologue_small_kernel<32, false>);
+    return launch_status();
+}
+
+int il_layernorm_backward(const float* gy, const float* x, const float* gamma, const float* mean, const float* rstd,
+                          float* dx, float* dgamma, float* dbeta, int64_t N, int64_t IN, void* stream) {
+    if (N < 0 || IN < 1 || IN > il::kCdfMaxIn || N > INT32_MAX) return IL_ERR_SHAPE;
+    if (N > 0 && (!gy || !x || !gamma || !mean || !rstd)) return IL_ERR_NULL;
+    int sms = 0;
+    int st = check_device(&sms);
+    if (st) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (dgamma && cudaMemsetAsync(dgamma, 0, (size_t)IN * sizeof(float), s) != cudaSuccess) return IL_ERR_LAUNCH;
+    if (dbeta && cudaMemsetAsync(dbeta, 0, (size_t)IN * sizeof(float), s) != cudaSuccess) return IL_ERR_LAUNCH;
+    if (N == 0 || (!dx && !dgamma && !dbeta)) return IL_OK;
+    const int vec = (IN % 4 == 0) && ((((uintptr_t)gy | (uintptr_t)x | (uintptr_t)dx) & 15) == 0);
+    // one wave, several tokens per thread: the block reduction runs once per block
+    const int64_t want = (N + il::kCdfRowThreads - 1) / il::kCdfRowThreads;
+    const unsigned blocks = (unsigned)std::min<int64_t>(want, (int64_t)sms);
+    auto run = [&](auto kern) {
+        kern<<<blocks, il::kCdfRowThreads, 0, s>>>(gy, x, gamma, nullptr, mean, rstd, dx, dgamma, dbeta, (int)N,
+                                                   (int)IN, vec);
+    };
+    if (IN <= 8) run(il::cdf_backward_small_kernel<8, false>);
+    else if (IN <= 16) run(il::cdf_backward_small_kernel<16, false>);
+    else if (IN <= 24) run(il::cdf_backward_small_kernel<24, false>);
+    else run(il::cdf_backward_small_kernel<32, false>);
+    return launch_status();
+}
+
 int64_t il_workspace_bytes(int64_t N, int64_t IN, int64_t OUT, int64_t K, int x_dtype) {
     return il::fast_backward_workspace(N, IN, OUT, K, x_dtype);
 }

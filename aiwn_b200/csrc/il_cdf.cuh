@@ -227,8 +227,9 @@ __global__ void __launch_bounds__(kCdfRowThreads) cdf_prologue_kernel(const floa
 }
 
 // The prologue for in_d <= MAXIN with the row in registers and 16-byte loads
-// and stores when rows are 4-aligned.
-template <int MAXIN>
+// and stores when rows are 4-aligned.  With CDF = false it is a plain
+// LayerNorm: xn receives the affine output (x - mean) * rstd * gamma + beta.
+template <int MAXIN, bool CDF = true>
 __global__ void __launch_bounds__(kCdfRowThreads)
     cdf_prologue_small_kernel(const float* x, CdfArgs q, int N, int IN, int vec) {
     const int n = blockIdx.x * kCdfRowThreads + threadIdx.x;
@@ -252,7 +253,13 @@ __global__ void __launch_bounds__(kCdfRowThreads)
     q.rstd[n] = rstd;
 #pragma unroll
     for (int k = 0; k < MAXIN; ++k)
-        if (k < IN) v[k] = cdf_map(v[k], mean, rstd, __ldg(q.gamma + k), __ldg(q.beta + k));
+        if (k < IN) {
+            if constexpr (CDF)
+                v[k] = cdf_map(v[k], mean, rstd, __ldg(q.gamma + k), __ldg(q.beta + k));
+            else
+                v[k] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[k], mean), rstd), __ldg(q.gamma + k)),
+                                 __ldg(q.beta + k));
+        }
     float* o = q.xn + (int64_t)n * IN;
     if (vec) {
 #pragma unroll
@@ -319,7 +326,9 @@ __global__ void __launch_bounds__(kCdfRowThreads)
 // pass per token (16-byte loads when rows are 4-aligned), a grid-stride loop
 // over tokens, dgamma / dbeta partial sums in registers, reduced over the warp
 // by shuffles and over the block with one shared atomic per warp and column.
-template <int MAXIN>
+// With CDF = false it is a plain LayerNorm's backward: gxn is the gradient of
+// the affine output itself (beta is not read).
+template <int MAXIN, bool CDF = true>
 __global__ void __launch_bounds__(kCdfRowThreads)
     cdf_backward_small_kernel(const float* gxn, const float* x, const float* gamma, const float* beta,
                               const float* mean, const float* rstd, float* dx, float* dgamma, float* dbeta, int N,
@@ -329,7 +338,7 @@ __global__ void __launch_bounds__(kCdfRowThreads)
     for (int k = threadIdx.x; k < 2 * MAXIN; k += kCdfRowThreads) sacc[k] = 0.f;
     for (int k = threadIdx.x; k < IN; k += kCdfRowThreads) {
         sgb[k] = gamma[k];
-        sgb[MAXIN + k] = beta[k];
+        sgb[MAXIN + k] = CDF ? beta[k] : 0.f;
     }
     __syncthreads();
     float ag[MAXIN], ab[MAXIN];
@@ -363,10 +372,13 @@ __global__ void __launch_bounds__(kCdfRowThreads)
         for (int k = 0; k < MAXIN; ++k) {
             if (k < IN) {
                 const float xh = __fmul_rn(__fsub_rn(xv[k], m), rs);
-                const float z = __fadd_rn(__fmul_rn(xh, sgb[k]), sgb[MAXIN + k]);
-                const float sv = __fdiv_rn(z, kSqrt2F);
-                const float dz =
-                    __fdiv_rn(__fmul_rn(__fmul_rn(gv[k], 1.12837916709551257f), expf(-__fmul_rn(sv, sv))), kSqrt2F);
+                float dz = gv[k];
+                if constexpr (CDF) {
+                    const float z = __fadd_rn(__fmul_rn(xh, sgb[k]), sgb[MAXIN + k]);
+                    const float sv = __fdiv_rn(z, kSqrt2F);
+                    dz = __fdiv_rn(__fmul_rn(__fmul_rn(gv[k], 1.12837916709551257f), expf(-__fmul_rn(sv, sv))),
+                                   kSqrt2F);
+                }
                 const float dxh = __fmul_rn(dz, sgb[k]);
                 s1 += dxh;
                 s2 += dxh * xh;

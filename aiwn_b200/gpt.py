@@ -8,7 +8,8 @@ up, down}} / ln_f``, ``lm_head``), so its state_dicts load unchanged.  The
 FFN's GaussianCDFNorm -> up pair runs as one IndexedLinearV2 chain
 (``il_cdf_forward``: the prologue fused into the forward when its output fits
 one j-range); every other IndexedLinear runs the library's forward and
-backward kernels.
+backward kernels, and the blocks' LayerNorms (d_idx <= 32) run
+``il_layernorm_forward`` / ``il_layernorm_backward``.
 
 At the reference's config-5 sizes (n_embd 256, K=128 -> d_idx 16, ff_idx 8;
 batch 64 x ctx 256) every kernel is small and the eager step is bound by
@@ -24,9 +25,50 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import _lib
 from .layers import GaussianCDFNorm, IndexedLinear
 from .layers.indexed_linear import TRITON_OK
 from .layers.indexed_linear_v2 import _FnV2
+
+
+class _LayerNormFn(torch.autograd.Function):
+    """LayerNorm over the last dim for d <= 32 through il_layernorm_forward /
+    il_layernorm_backward (fp32, one token per thread, rows in registers)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        n = x2.shape[0]
+        y = torch.empty_like(x2)
+        mean, rstd = x2.new_empty(n), x2.new_empty(n)
+        _lib.layernorm_forward(x2, weight, bias, eps, y, mean, rstd)
+        ctx.save_for_backward(x2, weight, mean, rstd)
+        ctx.shape = shape
+        return y.reshape(shape)
+
+    @staticmethod
+    def backward(ctx, gy):
+        x2, weight, mean, rstd = ctx.saved_tensors
+        gy2 = gy.reshape(x2.shape).contiguous()
+        dx = torch.empty_like(x2) if ctx.needs_input_grad[0] else None
+        dw = torch.empty_like(weight) if ctx.needs_input_grad[1] else None
+        db = torch.empty_like(weight) if ctx.needs_input_grad[2] else None
+        _lib.layernorm_backward(gy2, x2, weight, mean, rstd, dx, dw, db)
+        return (dx.reshape(ctx.shape) if dx is not None else None), dw, db, None
+
+
+def layer_norm(ln: nn.LayerNorm, x: torch.Tensor) -> torch.Tensor:
+    """``ln(x)`` with the library's kernels where they apply (fp32 CUDA
+    input, one normalised dim of at most 32, affine, no hooks on ``ln``);
+    torch's LayerNorm otherwise.  The IndexedGPT blocks' d_idx is 16 at the
+    reference's config 5, where torch's backward spends ~77 us per call on
+    the gamma/beta reduction of 16-wide rows."""
+    if (len(ln.normalized_shape) == 1 and ln.normalized_shape[0] <= 32 and ln.weight is not None
+            and ln.bias is not None and x.is_cuda and x.dtype == torch.float32
+            and not (ln._forward_pre_hooks or ln._forward_hooks)):
+        return _LayerNormFn.apply(x, ln.weight, ln.bias, ln.eps)
+    return ln(x)
 
 
 def get_d_idx(n_embd: int, K: int, n_head: int) -> tuple:
@@ -114,8 +156,8 @@ class IndexedBlock(nn.Module):
         self.ffn = IndexedFFN(d_idx, ff_idx, K, dropout)
 
     def forward(self, x):
-        x = x + self.attn(self.ln1(x))
-        x = x + self.ffn(self.ln2(x))
+        x = x + self.attn(layer_norm(self.ln1, x))
+        x = x + self.ffn(layer_norm(self.ln2, x))
         return x
 
 
@@ -163,7 +205,7 @@ class IndexedGPT(nn.Module):
                                      self.transformer["wpe"](torch.arange(T, device=idx.device)))
         for block in self.transformer["h"]:
             x = block(x)
-        x = self.transformer["ln_f"](x)
+        x = layer_norm(self.transformer["ln_f"], x)
         logits = self.lm_head(x)
         loss = None
         if targets is not None:

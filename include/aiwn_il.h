@@ -151,6 +151,24 @@ IL_API int il_cdf_forward(const float* x, const float* gamma, const float* beta,
                    int64_t OUT, int64_t K, double bw, void* stream);
 
 /*
+ * LayerNorm over the last dimension for in_d = IN <= 32 (fp32, biased
+ * variance, elementwise affine): y = (x - mean) * rstd * gamma + beta with
+ * rstd = 1/sqrt(var + eps); also writes mean and rstd [N] for the backward.
+ * Replaces torch.nn.LayerNorm(d_idx) in the reference's IndexedGPT blocks
+ * (transformer_validation.py:297-298, 329), whose d_idx is 16 at config 5.
+ */
+IL_API int il_layernorm_forward(const float* x, const float* gamma, const float* beta, double eps, float* y,
+                         float* mean, float* rstd, int64_t N, int64_t IN, void* stream);
+
+/*
+ * Backward of il_layernorm_forward given gy = dL/dy: writes dx [N, IN] and
+ * overwrites dgamma, dbeta [IN] (any of the three may be NULL).  IN <= 32.
+ */
+IL_API int il_layernorm_backward(const float* gy, const float* x, const float* gamma, const float* mean,
+                          const float* rstd, float* dx, float* dgamma, float* dbeta, int64_t N, int64_t IN,
+                          void* stream);
+
+/*
  * Backward of the GaussianCDFNorm prologue: given gxn = dL/dxn (from
  * il_backward run on xn), writes dx [N, IN] and overwrites dgamma, dbeta [IN].
  * Any of dx / dgamma / dbeta may be NULL.  IN <= 16384.  PyTorch autograd's

@@ -90,6 +90,18 @@ def test_cdf_entry_points_argument_checks():
     assert lib.il_cdf_backward(None, p, p, p, p, p, p, p, p, 4, 8, None) == 6
 
 
+def test_layernorm_entry_points_argument_checks():
+    """il_layernorm_forward / il_layernorm_backward reject bad arguments before touching a device."""
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    assert lib.il_layernorm_forward(None, None, None, 1e-5, None, None, None, 0, 16, None) == 0  # empty batch
+    assert lib.il_layernorm_forward(p, p, p, 1e-5, p, p, p, 4, 33, None) == 1  # in_d beyond 32
+    assert lib.il_layernorm_forward(p, p, p, -1.0, p, p, p, 4, 16, None) == 9  # negative eps
+    assert lib.il_layernorm_forward(p, None, p, 1e-5, p, p, p, 4, 16, None) == 6  # NULL gamma
+    assert lib.il_layernorm_backward(p, p, p, p, p, p, p, p, 4, 0, None) == 1
+    assert lib.il_layernorm_backward(None, p, p, p, p, p, p, p, 4, 16, None) == 6
+
+
 def test_bin_counts_argument_checks():
     lib = _lib.load()
     p = ctypes.c_void_p(16)
