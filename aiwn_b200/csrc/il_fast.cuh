@@ -450,7 +450,9 @@ inline int tokens_per_tile(int C) {
     return (R >= 32 ? 1 : 32 / R) * kWarps * kSlots;
 }
 
-inline bool plan_forward(int K, int IN, int OUT, FwdPlan& pl) {
+// min_cs > 1 asks for clusters of at least min_cs CTAs (fewer input columns
+// each), which spreads a small batch over more SMs
+inline bool plan_forward(int K, int IN, int OUT, FwdPlan& pl, int min_cs = 1) {
     const int chunks = OUT / 4;
     for (int C : kFwdChunks) {
         if (chunks % C != 0) continue;  // j-ranges tile OUT exactly
@@ -462,6 +464,7 @@ inline bool plan_forward(int K, int IN, int OUT, FwdPlan& pl) {
         // nb*KB rows from TMA (zero-filled past K) plus row K, rounded to 128 bytes
         const int slice = round_up(std::max(KB * nb, K + 1) * JR * 4, 128);
         for (int CS : {1, 2, 4, 8}) {
+            if (CS < min_cs) continue;
             const int IG = ceil_div(IN, CS);
             if (CS > 1 && (IG - 1) * CS >= IN) continue;  // every rank gets at least one column
             const int TT = tokens_per_tile(C);
@@ -581,6 +584,17 @@ inline int fast_forward(const void* x, int x_dtype, const float* table, const fl
                         cudaStream_t s) {
     FwdPlan pl;
     if (!plan_forward(c.K, (int)IN, (int)OUT, pl)) return kNotApplicable;
+    {
+        // too few token tiles to keep half the SMs busy: larger clusters, fewer
+        // columns per CTA (64x64, K=16 at 2 K tokens: 14.2 us with pairs, 9.4
+        // with clusters of 4, 11.1 with 8, whose 32 tiles take two rounds)
+        const int64_t tiles = ceil_div((int)N, tokens_per_tile(pl.C));
+        const int64_t jr = ceil_div((int)OUT, pl.JR);
+        int cs = pl.CS;
+        while (cs < 8 && 2 * tiles * jr * cs < num_sms) cs *= 2;
+        FwdPlan wide;
+        if (cs > pl.CS && plan_forward(c.K, (int)IN, (int)OUT, wide, cs) && wide.C == pl.C) pl = wide;
+    }
     CUtensorMap map;
     if (!make_table_map(&map, table, c.K, (int)IN, (int)OUT, pl.JR, pl.KB)) return kNotApplicable;
     FwdArgs a;
