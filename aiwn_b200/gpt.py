@@ -86,13 +86,20 @@ def get_d_idx(n_embd: int, K: int, n_head: int) -> tuple:
 
 
 class IndexedAttention(nn.Module):
-    """Causal multi-head attention with IndexedLinear q/k/v/c projections."""
+    """Causal multi-head attention with IndexedLinear q/k/v/c projections.
 
-    def __init__(self, d_idx, n_head, block_size, K, dropout=0.1):
+    ``fused=True`` computes softmax(mask(q k^T / sqrt(d))) v with dropout by
+    torch's scaled_dot_product_attention (no [B, H, T, T] tensors in memory);
+    ``fused=False`` keeps the reference's explicit masked-softmax formulation
+    (transformer_validation.py:264-267).  The two agree to fp32 rounding
+    without dropout; with dropout they draw different random masks."""
+
+    def __init__(self, d_idx, n_head, block_size, K, dropout=0.1, fused=True):
         super().__init__()
         assert d_idx % n_head == 0
         self.n_head = n_head
         self.d_idx = d_idx
+        self.fused = fused
         self.q_proj = IndexedLinear(d_idx, d_idx, K)
         self.k_proj = IndexedLinear(d_idx, d_idx, K)
         self.v_proj = IndexedLinear(d_idx, d_idx, K)
@@ -111,10 +118,15 @@ class IndexedAttention(nn.Module):
         k = k.view(B, T, self.n_head, C // self.n_head).transpose(1, 2)
         q = q.view(B, T, self.n_head, C // self.n_head).transpose(1, 2)
         v = v.view(B, T, self.n_head, C // self.n_head).transpose(1, 2)
-        att = (q @ k.transpose(-2, -1)) * (1.0 / math.sqrt(k.size(-1)))
-        att = att.masked_fill(self.bias[:, :, :T, :T] == 0, float("-inf"))
-        att = self.attn_drop(F.softmax(att, dim=-1))
-        y = (att @ v).transpose(1, 2).contiguous().view(B, T, C)
+        if self.fused:
+            p = self.attn_drop.p if self.training else 0.0
+            y = F.scaled_dot_product_attention(q, k, v, dropout_p=p, is_causal=True)
+        else:
+            att = (q @ k.transpose(-2, -1)) * (1.0 / math.sqrt(k.size(-1)))
+            att = att.masked_fill(self.bias[:, :, :T, :T] == 0, float("-inf"))
+            att = self.attn_drop(F.softmax(att, dim=-1))
+            y = att @ v
+        y = y.transpose(1, 2).contiguous().view(B, T, C)
         h = self.c_proj(y.reshape(B * T, C)).reshape(B, T, C)
         return self.resid_drop(h)
 
@@ -148,11 +160,11 @@ class IndexedFFN(nn.Module):
 
 
 class IndexedBlock(nn.Module):
-    def __init__(self, d_idx, ff_idx, n_head, block_size, K, dropout=0.1):
+    def __init__(self, d_idx, ff_idx, n_head, block_size, K, dropout=0.1, fused_attention=True):
         super().__init__()
         self.ln1 = nn.LayerNorm(d_idx)
         self.ln2 = nn.LayerNorm(d_idx)
-        self.attn = IndexedAttention(d_idx, n_head, block_size, K, dropout)
+        self.attn = IndexedAttention(d_idx, n_head, block_size, K, dropout, fused=fused_attention)
         self.ffn = IndexedFFN(d_idx, ff_idx, K, dropout)
 
     def forward(self, x):
@@ -162,9 +174,12 @@ class IndexedBlock(nn.Module):
 
 
 class IndexedGPT(nn.Module):
-    """GPT with every linear op an IndexedLinear at d_idx (transformer_validation.py:295-385)."""
+    """GPT with every linear op an IndexedLinear at d_idx (transformer_validation.py:295-385).
+    The reference's constructor arguments; ``fused_attention`` (keyword, default
+    True) selects IndexedAttention's fused form."""
 
-    def __init__(self, vocab_size, block_size, n_layer, n_head, n_embd, K, dropout=0.1):
+    def __init__(self, vocab_size, block_size, n_layer, n_head, n_embd, K, dropout=0.1, *,
+                 fused_attention=True):
         super().__init__()
         self.block_size = block_size
         self.ffn_type = "indexed"
@@ -176,7 +191,7 @@ class IndexedGPT(nn.Module):
             "wte": nn.Embedding(vocab_size, d_idx),
             "wpe": nn.Embedding(block_size, d_idx),
             "drop": nn.Dropout(dropout),
-            "h": nn.ModuleList([IndexedBlock(d_idx, ff_idx, n_head, block_size, K, dropout)
+            "h": nn.ModuleList([IndexedBlock(d_idx, ff_idx, n_head, block_size, K, dropout, fused_attention)
                                 for _ in range(n_layer)]),
             "ln_f": nn.LayerNorm(d_idx),
         })

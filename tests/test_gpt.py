@@ -65,6 +65,30 @@ def test_forward_backward_match_reference():
 
 
 @pytest.mark.gpu
+def test_fused_attention_matches_explicit():
+    """IndexedAttention's fused form and the reference's explicit masked
+    softmax give the same loss and gradients without dropout."""
+    d = _golden()
+    x = torch.from_numpy(d["x"]).cuda()
+    y = torch.from_numpy(d["y"]).cuda()
+    m1 = _model(d, "cuda")
+    m2 = _model(d, "cuda")
+    for blk in m2.transformer["h"]:
+        blk.attn.fused = False
+    assert all(b.attn.fused for b in m1.transformer["h"])
+    _, l1 = m1(x, y)
+    _, l2 = m2(x, y)
+    l1.backward()
+    l2.backward()
+    assert abs(l1.item() - l2.item()) <= 1e-5 * abs(l2.item())
+    for (name, a), b in zip(m1.named_parameters(), m2.parameters()):
+        ga, gb = a.grad.cpu().numpy(), b.grad.cpu().numpy()
+        if np.abs(gb).max() < 1e-6:
+            continue  # the key bias: zero in exact arithmetic
+        normwise_close(ga, gb, 1e-4, name)
+
+
+@pytest.mark.gpu
 def test_graphed_train_step_matches_eager_training():
     d = _golden()
     x = torch.from_numpy(d["x"]).cuda()
