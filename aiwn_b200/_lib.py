@@ -64,6 +64,13 @@ def load():
         lib.il_layernorm_forward.restype = ci
         lib.il_layernorm_backward.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
         lib.il_layernorm_backward.restype = ci
+        lib.il_attention_forward.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, f64, f64, vp, vp]
+        lib.il_attention_forward.restype = ci
+        lib.il_attention_backward.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, f64, f64,
+                                              vp, vp]
+        lib.il_attention_backward.restype = ci
+        lib.il_attention_dropout_mask.argtypes = [vp, i64, i64, i64, f64, vp, vp]
+        lib.il_attention_dropout_mask.restype = ci
         lib.il_bin_counts.argtypes = [vp, ci, i64, i64, i64, f64, vp, vp]
         lib.il_bin_counts.restype = ci
         lib.il_kernel_launches.argtypes = []
@@ -211,6 +218,43 @@ def layernorm_backward(gy, x, gamma, mean, rstd, dx, dgamma, dbeta):
     with _on_device(x.device):
         _check(lib.il_layernorm_backward(_p(gy), _p(x), _p(gamma), _p(mean), _p(rstd), _p(dx), _p(dgamma),
                                          _p(dbeta), N, IN, _stream(x.device)), "il_layernorm_backward")
+
+
+def attention_supported(T: int, D: int) -> bool:
+    """Whether il_attention_* take heads of D features over T positions."""
+    return D in (2, 4, 8, 16) and 1 <= T <= (512 if D == 16 else 1024)
+
+
+def attention_forward(q, k, v, o, lse, H: int, scale: float, p: float, seed):
+    """o <- causal attention of fp32 q, k, v [B, T, H*D] (dropout p, device
+    int64 seed [1]); lse [B, H, T] for the backward."""
+    _need_cuda(q, k, v, o, lse, seed)
+    B, T, C = q.shape
+    lib = load()
+    with _on_device(q.device):
+        _check(lib.il_attention_forward(_p(q), _p(k), _p(v), _p(o), _p(lse), B, T, H, C // H, float(scale),
+                                        float(p), _p(seed), _stream(q.device)), "il_attention_forward")
+    return o
+
+
+def attention_backward(q, k, v, o, do, lse, dq, dk, dv, H: int, scale: float, p: float, seed):
+    """dq, dk, dv <- backward of attention_forward given do = dL/do."""
+    _need_cuda(q, k, v, o, do, lse, dq, dk, dv, seed)
+    B, T, C = q.shape
+    lib = load()
+    with _on_device(q.device):
+        _check(lib.il_attention_backward(_p(q), _p(k), _p(v), _p(o), _p(do), _p(lse), _p(dq), _p(dk), _p(dv), B, T,
+                                         H, C // H, float(scale), float(p), _p(seed), _stream(q.device)),
+               "il_attention_backward")
+
+
+def attention_dropout_mask(keep, B: int, T: int, H: int, p: float, seed):
+    """keep [B, H, T, T] uint8 <- the dropout mask attention_forward uses."""
+    _need_cuda(keep, seed)
+    lib = load()
+    with _on_device(keep.device):
+        _check(lib.il_attention_dropout_mask(_p(keep), B, T, H, float(p), _p(seed), _stream(keep.device)),
+               "il_attention_dropout_mask")
 
 
 def bin_counts(x, K: int, bw: float, counts):

@@ -1,0 +1,220 @@
+// il_attn.cuh -- causal self-attention for the narrow heads of IndexedGPT.
+//
+// IndexedGPT's blocks attend over d_idx / n_head = 4 features per head at the
+// reference's config 5 (transformer_validation.py:254-269).  Library kernels
+// for attention pad such heads to 32 or more features; here one CTA owns one
+// (batch, head), one thread one query row, and K and V of the head sit in
+// shared memory:
+//
+//   forward:  o_i = sum_{j<=i} softmax_j(q_i.k_j * scale) * keep_ij / (1-p) * v_j
+//             (online softmax over j), plus lse_i = log sum_j exp(s_ij)
+//   backward: Dsum_i = dO_i . o_i;  P_ij = exp(s_ij - lse_i);
+//             dS_ij = P_ij (keep_ij / (1-p) * dO_i.v_j - Dsum_i)
+//             dq_i = scale * sum_{j<=i} dS_ij k_j           (thread per query)
+//             dk_j = scale * sum_{i>=j} dS_ij q_i,
+//             dv_j = sum_{i>=j} P_ij keep_ij / (1-p) dO_i   (thread per key)
+//   so every backward thread runs i+1 + T-i iterations.
+//
+// q, k, v, o, dq, dk, dv are [B, T, H*D] (the projections' own layout: no
+// head transposes).  Dropout keeps element (b, h, i, j) when the top 32 bits
+// of splitmix64 (Steele, Lea and Flood, 2014) of seed + index * golden-ratio
+// constant reach p * 2^32; the backward regenerates the same mask from the
+// same device-resident seed.
+#pragma once
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+namespace il {
+
+constexpr int kAttnMaxT = 1024;
+// the 16-feature backward keeps more state per thread: at most 512 positions
+__host__ __device__ constexpr int attn_max_t(int D) { return D >= 16 ? 512 : kAttnMaxT; }
+
+__device__ __forceinline__ bool attn_keep(uint64_t seed, uint64_t idx, uint32_t thr) {
+    uint64_t z = seed + idx * 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    return (uint32_t)(z >> 32) >= thr;
+}
+
+template <int D>
+__device__ __forceinline__ void attn_load_row(const float* s, float (&r)[D]) {
+    if constexpr (D % 4 == 0) {
+#pragma unroll
+        for (int d = 0; d < D; d += 4) {
+            const float4 t = *reinterpret_cast<const float4*>(s + d);
+            r[d] = t.x, r[d + 1] = t.y, r[d + 2] = t.z, r[d + 3] = t.w;
+        }
+    } else {
+#pragma unroll
+        for (int d = 0; d < D; ++d) r[d] = s[d];
+    }
+}
+
+template <int D>
+__device__ __forceinline__ float attn_dot(const float (&a)[D], const float (&b)[D]) {
+    float s = 0.f;
+#pragma unroll
+    for (int d = 0; d < D; ++d) s = fmaf(a[d], b[d], s);
+    return s;
+}
+
+// grid (H, B), block T threads; dynamic shared memory 2*T*D floats
+template <int D>
+__global__ void __launch_bounds__(kAttnMaxT)
+    attn_fwd_kernel(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+                    float* __restrict__ o, float* __restrict__ lse, int T, int H, float scale, uint32_t thr,
+                    float inv_keep, const uint64_t* __restrict__ seedp) {
+    extern __shared__ float sm[];
+    float* ks = sm;
+    float* vs = sm + T * D;
+    const int h = blockIdx.x, b = blockIdx.y, i = threadIdx.x;
+    const int HD = H * D;
+    const int64_t base = (int64_t)b * T * HD + (int64_t)h * D;
+    for (int e = threadIdx.x; e < T * D; e += blockDim.x) {
+        const int t = e / D, d = e - t * D;
+        ks[e] = k[base + (int64_t)t * HD + d];
+        vs[e] = v[base + (int64_t)t * HD + d];
+    }
+    __syncthreads();
+    const uint64_t seed = thr ? *seedp : 0ull;
+    float qi[D], acc[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d) {
+        qi[d] = q[base + (int64_t)i * HD + d];
+        acc[d] = 0.f;
+    }
+    float m = -INFINITY, l = 0.f;
+    const uint64_t row = ((uint64_t)(b * H + h) * (uint64_t)T + (uint64_t)i) * (uint64_t)T;
+    for (int j = 0; j <= i; ++j) {
+        float kj[D], vj[D];
+        attn_load_row<D>(ks + j * D, kj);
+        const float s = attn_dot<D>(qi, kj) * scale;
+        if (s > m) {  // rescale the running sums to the new maximum
+            const float c = expf(m - s);
+            l *= c;
+#pragma unroll
+            for (int d = 0; d < D; ++d) acc[d] *= c;
+            m = s;
+        }
+        const float e = expf(s - m);
+        l += e;
+        if (thr == 0u || attn_keep(seed, row + (uint64_t)j, thr)) {
+            attn_load_row<D>(vs + j * D, vj);
+#pragma unroll
+            for (int d = 0; d < D; ++d) acc[d] = fmaf(e, vj[d], acc[d]);
+        }
+    }
+    const float r = inv_keep / l;
+#pragma unroll
+    for (int d = 0; d < D; ++d) o[base + (int64_t)i * HD + d] = acc[d] * r;
+    lse[(int64_t)(b * H + h) * T + i] = m + logf(l);
+}
+
+// grid (H, B), block T threads; dynamic shared memory (4*T*D + 2*T) floats
+template <int D>
+__global__ void __launch_bounds__(attn_max_t(D))
+    attn_bwd_kernel(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+                    const float* __restrict__ o, const float* __restrict__ dout, const float* __restrict__ lse,
+                    float* __restrict__ dq, float* __restrict__ dk, float* __restrict__ dv, int T, int H,
+                    float scale, uint32_t thr, float inv_keep, const uint64_t* __restrict__ seedp) {
+    extern __shared__ float sm[];
+    float* qs = sm;
+    float* ks = qs + T * D;
+    float* vs = ks + T * D;
+    float* dos = vs + T * D;
+    float* ls = dos + T * D;
+    float* dsum = ls + T;
+    const int h = blockIdx.x, b = blockIdx.y, t0 = threadIdx.x;
+    const int HD = H * D;
+    const int64_t base = (int64_t)b * T * HD + (int64_t)h * D;
+    for (int e = threadIdx.x; e < T * D; e += blockDim.x) {
+        const int t = e / D, d = e - t * D;
+        const int64_t at = base + (int64_t)t * HD + d;
+        qs[e] = q[at];
+        ks[e] = k[at];
+        vs[e] = v[at];
+        dos[e] = dout[at];
+    }
+    {
+        float s = 0.f;
+#pragma unroll
+        for (int d = 0; d < D; ++d) {
+            const int64_t at = base + (int64_t)t0 * HD + d;
+            s = fmaf(dout[at], o[at], s);
+        }
+        dsum[t0] = s;
+        ls[t0] = lse[(int64_t)(b * H + h) * T + t0];
+    }
+    __syncthreads();
+    const uint64_t seed = thr ? *seedp : 0ull;
+    const uint64_t bh = (uint64_t)(b * H + h) * (uint64_t)T;
+    // dq: this thread's query i = t0, keys j <= i
+    {
+        const int i = t0;
+        float qi[D], doi[D], g[D];
+        attn_load_row<D>(qs + i * D, qi);
+        attn_load_row<D>(dos + i * D, doi);
+#pragma unroll
+        for (int d = 0; d < D; ++d) g[d] = 0.f;
+        const float li = ls[i], di = dsum[i];
+        const uint64_t row = (bh + (uint64_t)i) * (uint64_t)T;
+        for (int j = 0; j <= i; ++j) {
+            float kj[D], vj[D];
+            attn_load_row<D>(ks + j * D, kj);
+            attn_load_row<D>(vs + j * D, vj);
+            const float p = expf(attn_dot<D>(qi, kj) * scale - li);
+            const bool keep = thr == 0u || attn_keep(seed, row + (uint64_t)j, thr);
+            const float dp = keep ? attn_dot<D>(doi, vj) * inv_keep : 0.f;
+            const float ds = p * (dp - di);
+#pragma unroll
+            for (int d = 0; d < D; ++d) g[d] = fmaf(ds, kj[d], g[d]);
+        }
+#pragma unroll
+        for (int d = 0; d < D; ++d) dq[base + (int64_t)i * HD + d] = g[d] * scale;
+    }
+    // dk, dv: this thread's key j = t0, queries i >= j
+    {
+        const int j = t0;
+        float kj[D], vj[D], gk[D], gv[D];
+        attn_load_row<D>(ks + j * D, kj);
+        attn_load_row<D>(vs + j * D, vj);
+#pragma unroll
+        for (int d = 0; d < D; ++d) gk[d] = gv[d] = 0.f;
+        for (int i = j; i < T; ++i) {
+            float qi[D], doi[D];
+            attn_load_row<D>(qs + i * D, qi);
+            attn_load_row<D>(dos + i * D, doi);
+            const float p = expf(attn_dot<D>(qi, kj) * scale - ls[i]);
+            const bool keep = thr == 0u || attn_keep(seed, (bh + (uint64_t)i) * (uint64_t)T + (uint64_t)j, thr);
+            const float z = keep ? p * inv_keep : 0.f;
+            const float dp = keep ? attn_dot<D>(doi, vj) * inv_keep : 0.f;
+            const float ds = p * (dp - dsum[i]);
+#pragma unroll
+            for (int d = 0; d < D; ++d) {
+                gv[d] = fmaf(z, doi[d], gv[d]);
+                gk[d] = fmaf(ds, qi[d], gk[d]);
+            }
+        }
+#pragma unroll
+        for (int d = 0; d < D; ++d) {
+            dk[base + (int64_t)j * HD + d] = gk[d] * scale;
+            dv[base + (int64_t)j * HD + d] = gv[d];
+        }
+    }
+}
+
+// keep[b, h, i, j] (1 = kept) of the dropout mask, for the tests
+__global__ void attn_mask_kernel(uint8_t* keep, int64_t n, int T, uint32_t thr, const uint64_t* seedp) {
+    const uint64_t seed = *seedp;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x)
+        keep[e] = attn_keep(seed, (uint64_t)e, thr) ? 1 : 0;
+    (void)T;
+}
+
+inline int64_t attn_fwd_smem(int T, int D) { return (int64_t)2 * T * D * 4; }
+inline int64_t attn_bwd_smem(int T, int D) { return ((int64_t)4 * T * D + 2 * T) * 4; }
+
+}  // namespace il

@@ -20,6 +20,7 @@
 #include "il_sorted.cuh"
 #include "il_fwd_token.cuh"
 #include "il_cdf.cuh"
+#include "il_attn.cuh"
 
 namespace {
 
@@ -165,6 +166,32 @@ int forward_dispatch(const void* x, int x_dtype, const float* table, const float
         il::fwd_simple_kernel<il::kBF16><<<g, 256, 0, s>>>(x, table, bias, out, N, IN, OUT, c);
     else
         il::fwd_simple_kernel<il::kF32><<<g, 256, 0, s>>>(x, table, bias, out, N, IN, OUT, c);
+    return launch_status();
+}
+
+// shape, dropout and seed checks shared by the attention entry points
+int attn_check(int64_t B, int64_t T, int64_t H, int64_t D, double p, const uint64_t* seed, bool bwd) {
+    if (B < 1 || B > 65535 || H < 1 || H > 65535 || T < 1 || T > il::kAttnMaxT) return IL_ERR_SHAPE;
+    if (D != 2 && D != 4 && D != 8 && D != 16) return IL_ERR_SHAPE;
+    if (T > il::attn_max_t((int)D)) return IL_ERR_SHAPE;
+    if ((bwd ? il::attn_bwd_smem((int)T, (int)D) : il::attn_fwd_smem((int)T, (int)D)) > 227 * 1024)
+        return IL_ERR_SHAPE;
+    if (!(p >= 0.0 && p < 1.0)) return IL_ERR_VALUE;
+    if (p > 0.0 && !seed) return IL_ERR_NULL;
+    return IL_OK;
+}
+
+uint32_t attn_threshold(double p) {
+    const double t = p * 4294967296.0;
+    return p <= 0.0 ? 0u : (t >= 4294967295.0 ? 4294967295u : (uint32_t)t);
+}
+
+template <typename Kern, typename... Args>
+int attn_launch(Kern kern, int64_t smem, int64_t B, int64_t T, int64_t H, cudaStream_t s, Args... args) {
+    if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+                                cudaSuccess)
+        return IL_ERR_LAUNCH;
+    kern<<<dim3((unsigned)H, (unsigned)B, 1), (unsigned)T, (size_t)smem, s>>>(args...);
     return launch_status();
 }
 
@@ -334,6 +361,63 @@ int il_layernorm_backward(const float* gy, const float* x, const float* gamma, c
     else if (IN <= 16) run(il::cdf_backward_small_kernel<16, false>);
     else if (IN <= 24) run(il::cdf_backward_small_kernel<24, false>);
     else run(il::cdf_backward_small_kernel<32, false>);
+    return launch_status();
+}
+
+int il_attention_forward(const float* q, const float* k, const float* v, float* o, float* lse, int64_t B,
+                         int64_t T, int64_t H, int64_t D, double scale, double p, const uint64_t* seed,
+                         void* stream) {
+    int st = attn_check(B, T, H, D, p, seed, false);
+    if (st) return st;
+    if (!q || !k || !v || !o || !lse) return IL_ERR_NULL;
+    int sms = 0;
+    if ((st = check_device(&sms))) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    const uint32_t thr = attn_threshold(p);
+    const float inv_keep = (float)(1.0 / (1.0 - p));
+    const int64_t smem = il::attn_fwd_smem((int)T, (int)D);
+    const int t = (int)T, h = (int)H;
+    const float sc = (float)scale;
+    switch (D) {
+        case 2: return attn_launch(il::attn_fwd_kernel<2>, smem, B, T, H, s, q, k, v, o, lse, t, h, sc, thr, inv_keep, seed);
+        case 4: return attn_launch(il::attn_fwd_kernel<4>, smem, B, T, H, s, q, k, v, o, lse, t, h, sc, thr, inv_keep, seed);
+        case 8: return attn_launch(il::attn_fwd_kernel<8>, smem, B, T, H, s, q, k, v, o, lse, t, h, sc, thr, inv_keep, seed);
+        default: return attn_launch(il::attn_fwd_kernel<16>, smem, B, T, H, s, q, k, v, o, lse, t, h, sc, thr, inv_keep, seed);
+    }
+}
+
+int il_attention_backward(const float* q, const float* k, const float* v, const float* o, const float* dout,
+                          const float* lse, float* dq, float* dk, float* dv, int64_t B, int64_t T, int64_t H,
+                          int64_t D, double scale, double p, const uint64_t* seed, void* stream) {
+    int st = attn_check(B, T, H, D, p, seed, true);
+    if (st) return st;
+    if (!q || !k || !v || !o || !dout || !lse || !dq || !dk || !dv) return IL_ERR_NULL;
+    int sms = 0;
+    if ((st = check_device(&sms))) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    const uint32_t thr = attn_threshold(p);
+    const float inv_keep = (float)(1.0 / (1.0 - p));
+    const int64_t smem = il::attn_bwd_smem((int)T, (int)D);
+    const int t = (int)T, h = (int)H;
+    const float sc = (float)scale;
+    switch (D) {
+        case 2: return attn_launch(il::attn_bwd_kernel<2>, smem, B, T, H, s, q, k, v, o, dout, lse, dq, dk, dv, t, h, sc, thr, inv_keep, seed);
+        case 4: return attn_launch(il::attn_bwd_kernel<4>, smem, B, T, H, s, q, k, v, o, dout, lse, dq, dk, dv, t, h, sc, thr, inv_keep, seed);
+        case 8: return attn_launch(il::attn_bwd_kernel<8>, smem, B, T, H, s, q, k, v, o, dout, lse, dq, dk, dv, t, h, sc, thr, inv_keep, seed);
+        default: return attn_launch(il::attn_bwd_kernel<16>, smem, B, T, H, s, q, k, v, o, dout, lse, dq, dk, dv, t, h, sc, thr, inv_keep, seed);
+    }
+}
+
+int il_attention_dropout_mask(uint8_t* keep, int64_t B, int64_t T, int64_t H, double p, const uint64_t* seed,
+                              void* stream) {
+    int st = attn_check(B, T, H, 4, p, seed, false);
+    if (st) return st;
+    if (!keep || !seed) return IL_ERR_NULL;
+    int sms = 0;
+    if ((st = check_device(&sms))) return st;
+    const int64_t n = B * H * T * T;
+    il::attn_mask_kernel<<<grid_for(n, 256, sms), 256, 0, (cudaStream_t)stream>>>(keep, n, (int)T,
+                                                                                  attn_threshold(p), seed);
     return launch_status();
 }
 

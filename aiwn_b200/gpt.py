@@ -58,6 +58,30 @@ class _LayerNormFn(torch.autograd.Function):
         return (dx.reshape(ctx.shape) if dx is not None else None), dw, db, None
 
 
+class _AttentionFn(torch.autograd.Function):
+    """Causal attention of q, k, v [B, T, H*D] through il_attention_forward /
+    il_attention_backward (narrow heads, dropout p with a device seed)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, H, p, seed):
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        B, T, C = q.shape
+        scale = 1.0 / math.sqrt(C // H)
+        o = torch.empty_like(q)
+        lse = q.new_empty(B, H, T)
+        _lib.attention_forward(q, k, v, o, lse, H, scale, p, seed)
+        ctx.save_for_backward(q, k, v, o, lse, seed)
+        ctx.H, ctx.p, ctx.scale = H, p, scale
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse, seed = ctx.saved_tensors
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        _lib.attention_backward(q, k, v, o, do.contiguous(), lse, dq, dk, dv, ctx.H, ctx.scale, ctx.p, seed)
+        return dq, dk, dv, None, None, None
+
+
 def layer_norm(ln: nn.LayerNorm, x: torch.Tensor) -> torch.Tensor:
     """``ln(x)`` with the library's kernels where they apply (fp32 CUDA
     input, one normalised dim of at most 32, affine, no hooks on ``ln``);
@@ -88,11 +112,14 @@ def get_d_idx(n_embd: int, K: int, n_head: int) -> tuple:
 class IndexedAttention(nn.Module):
     """Causal multi-head attention with IndexedLinear q/k/v/c projections.
 
-    ``fused=True`` computes softmax(mask(q k^T / sqrt(d))) v with dropout by
-    torch's scaled_dot_product_attention (no [B, H, T, T] tensors in memory);
+    ``fused=True`` computes softmax(mask(q k^T / sqrt(d))) v with dropout
+    without [B, H, T, T] tensors in memory: through il_attention_forward /
+    backward for fp32 CUDA heads of 2, 4, 8 or 16 features (the dropout seed
+    lives on the device and advances every training forward, so CUDA graph
+    replays draw new masks), else torch's scaled_dot_product_attention.
     ``fused=False`` keeps the reference's explicit masked-softmax formulation
-    (transformer_validation.py:264-267).  The two agree to fp32 rounding
-    without dropout; with dropout they draw different random masks."""
+    (transformer_validation.py:264-267).  They agree to fp32 rounding without
+    dropout; with dropout they draw different random masks."""
 
     def __init__(self, d_idx, n_head, block_size, K, dropout=0.1, fused=True):
         super().__init__()
@@ -100,6 +127,7 @@ class IndexedAttention(nn.Module):
         self.n_head = n_head
         self.d_idx = d_idx
         self.fused = fused
+        self._attn_seed = None  # device int64 [1], drawn from the CUDA generator on first use
         self.q_proj = IndexedLinear(d_idx, d_idx, K)
         self.k_proj = IndexedLinear(d_idx, d_idx, K)
         self.v_proj = IndexedLinear(d_idx, d_idx, K)
@@ -115,6 +143,18 @@ class IndexedAttention(nn.Module):
         q = self.q_proj(h).reshape(B, T, self.d_idx)
         k = self.k_proj(h).reshape(B, T, self.d_idx)
         v = self.v_proj(h).reshape(B, T, self.d_idx)
+        D = C // self.n_head
+        if self.fused and q.is_cuda and q.dtype == torch.float32 and _lib.attention_supported(T, D):
+            p = self.attn_drop.p if self.training else 0.0
+            if self._attn_seed is None or self._attn_seed.device != q.device:
+                self._attn_seed = torch.randint(0, 2 ** 62, (1,), dtype=torch.int64, device=q.device)
+            seed = self._attn_seed
+            if p > 0.0:
+                seed = self._attn_seed.clone()
+                self._attn_seed.add_(1)  # on the device: graph replays advance it too
+            y = _AttentionFn.apply(q, k, v, self.n_head, p, seed)
+            h = self.c_proj(y.reshape(B * T, C)).reshape(B, T, C)
+            return self.resid_drop(h)
         k = k.view(B, T, self.n_head, C // self.n_head).transpose(1, 2)
         q = q.view(B, T, self.n_head, C // self.n_head).transpose(1, 2)
         v = v.view(B, T, self.n_head, C // self.n_head).transpose(1, 2)

@@ -169,6 +169,30 @@ IL_API int il_layernorm_backward(const float* gy, const float* x, const float* g
                           void* stream);
 
 /*
+ * Causal self-attention of the IndexedGPT blocks (transformer_validation.py:
+ * 254-269: softmax(mask(q k^T * scale)) with dropout p, times v) for heads of
+ * D = 2, 4, 8 or 16 features, T <= 1024 positions (512 for D = 16).  q, k, v, o are fp32
+ * [B, T, H*D] (head h in columns h*D..h*D+D-1); lse [B, H, T] receives the
+ * log-sum-exp of each query's scores for the backward.  With p > 0, *seed
+ * (device memory) selects the dropout mask; the backward must get the same
+ * seed.  Element (b, h, i, j) is kept when the top 32 bits of splitmix64 of
+ * seed + index * 0x9E3779B97F4A7C15 are >= p * 2^32 (index = ((b*H+h)*T+i)*T+j).
+ */
+IL_API int il_attention_forward(const float* q, const float* k, const float* v, float* o, float* lse, int64_t B,
+                         int64_t T, int64_t H, int64_t D, double scale, double p, const uint64_t* seed,
+                         void* stream);
+
+/* Backward of il_attention_forward given dout = dL/do: writes dq, dk, dv. */
+IL_API int il_attention_backward(const float* q, const float* k, const float* v, const float* o,
+                          const float* dout, const float* lse, float* dq, float* dk, float* dv, int64_t B,
+                          int64_t T, int64_t H, int64_t D, double scale, double p, const uint64_t* seed,
+                          void* stream);
+
+/* The dropout mask of il_attention_forward as keep[B, H, T, T] (1 = kept), for tests. */
+IL_API int il_attention_dropout_mask(uint8_t* keep, int64_t B, int64_t T, int64_t H, double p,
+                              const uint64_t* seed, void* stream);
+
+/*
  * Backward of the GaussianCDFNorm prologue: given gxn = dL/dxn (from
  * il_backward run on xn), writes dx [N, IN] and overwrites dgamma, dbeta [IN].
  * Any of dx / dgamma / dbeta may be NULL.  IN <= 16384.  PyTorch autograd's

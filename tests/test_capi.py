@@ -102,6 +102,19 @@ def test_layernorm_entry_points_argument_checks():
     assert lib.il_layernorm_backward(None, p, p, p, p, p, p, p, 4, 16, None) == 6
 
 
+def test_attention_entry_points_argument_checks():
+    """il_attention_* reject unsupported shapes and dropout values before touching a device."""
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    assert lib.il_attention_forward(p, p, p, p, p, 2, 256, 4, 3, 0.5, 0.0, None, None) == 1  # D = 3
+    assert lib.il_attention_forward(p, p, p, p, p, 2, 2048, 4, 4, 0.5, 0.0, None, None) == 1  # T > 1024
+    assert lib.il_attention_forward(p, p, p, p, p, 2, 600, 4, 16, 0.5, 0.0, None, None) == 1  # D = 16, T > 512
+    assert lib.il_attention_forward(p, p, p, p, p, 2, 256, 4, 4, 0.5, 1.0, p, None) == 9  # p >= 1
+    assert lib.il_attention_forward(p, p, p, p, p, 2, 256, 4, 4, 0.5, 0.1, None, None) == 6  # dropout, no seed
+    assert lib.il_attention_backward(p, p, p, p, p, p, p, p, p, 0, 256, 4, 4, 0.5, 0.0, None, None) == 1
+    assert _lib.attention_supported(256, 4) and not _lib.attention_supported(256, 5)
+
+
 def test_bin_counts_argument_checks():
     lib = _lib.load()
     p = ctypes.c_void_p(16)
