@@ -3,8 +3,8 @@
 // IndexedGPT's blocks attend over d_idx / n_head = 4 features per head at the
 // reference's config 5 (transformer_validation.py:254-269).  Library kernels
 // for attention pad such heads to 32 or more features; here one CTA owns one
-// (batch, head), one thread one query row, and K and V of the head sit in
-// shared memory:
+// (batch, head), a group of S lanes one query row, and K and V of the head sit in
+// shared memory, with S = 1, 2 or 4 lanes sharing a query (or key):
 //
 //   forward:  o_i = sum_{j<=i} softmax_j(q_i.k_j * scale) * keep_ij / (1-p) * v_j
 //             (online softmax over j), plus lse_i = log sum_j exp(s_ij)
@@ -13,7 +13,7 @@
 //             dq_i = scale * sum_{j<=i} dS_ij k_j           (thread per query)
 //             dk_j = scale * sum_{i>=j} dS_ij q_i,
 //             dv_j = sum_{i>=j} P_ij keep_ij / (1-p) dO_i   (thread per key)
-//   so every backward thread runs i+1 + T-i iterations.
+//   so every backward lane group runs i+1 + T-i iterations.
 //
 // q, k, v, o, dq, dk, dv are [B, T, H*D] (the projections' own layout: no
 // head transposes).  Dropout keeps element (b, h, i, j) when the top 32 bits
@@ -61,8 +61,32 @@ __device__ __forceinline__ float attn_dot(const float (&a)[D], const float (&b)[
     return s;
 }
 
-// grid (H, B), block T threads; dynamic shared memory 2*T*D floats
-template <int D>
+// S lanes share one query (forward, dq) or one key (dk, dv): lane r of a
+// group takes every S-th key or query from r on, and the group's partial
+// results are combined by shuffles.  Block = T*S threads.
+// lanes of this thread's warp that exist (the last warp of a block of T*S
+// threads may be partial; groups of S never straddle its end)
+__device__ __forceinline__ unsigned warp_lanes() {
+    const int n = min(32, (int)blockDim.x - ((int)threadIdx.x & ~31));
+    return n == 32 ? 0xffffffffu : ((1u << n) - 1u);
+}
+
+template <int S>
+__device__ __forceinline__ float group_sum(float v, unsigned lanes) {
+#pragma unroll
+    for (int o = 1; o < S; o <<= 1) v += __shfl_xor_sync(lanes, v, o);
+    return v;
+}
+
+template <int S>
+__device__ __forceinline__ float group_max(float v, unsigned lanes) {
+#pragma unroll
+    for (int o = 1; o < S; o <<= 1) v = fmaxf(v, __shfl_xor_sync(lanes, v, o));
+    return v;
+}
+
+// grid (H, B), block T*S threads; dynamic shared memory 2*T*D floats
+template <int D, int S>
 __global__ void __launch_bounds__(kAttnMaxT)
     attn_fwd_kernel(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
                     float* __restrict__ o, float* __restrict__ lse, int T, int H, float scale, uint32_t thr,
@@ -70,7 +94,8 @@ __global__ void __launch_bounds__(kAttnMaxT)
     extern __shared__ float sm[];
     float* ks = sm;
     float* vs = sm + T * D;
-    const int h = blockIdx.x, b = blockIdx.y, i = threadIdx.x;
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int i = (int)threadIdx.x / S, r = (int)threadIdx.x % S;
     const int HD = H * D;
     const int64_t base = (int64_t)b * T * HD + (int64_t)h * D;
     for (int e = threadIdx.x; e < T * D; e += blockDim.x) {
@@ -88,7 +113,7 @@ __global__ void __launch_bounds__(kAttnMaxT)
     }
     float m = -INFINITY, l = 0.f;
     const uint64_t row = ((uint64_t)(b * H + h) * (uint64_t)T + (uint64_t)i) * (uint64_t)T;
-    for (int j = 0; j <= i; ++j) {
+    for (int j = r; j <= i; j += S) {
         float kj[D], vj[D];
         attn_load_row<D>(ks + j * D, kj);
         const float s = attn_dot<D>(qi, kj) * scale;
@@ -107,14 +132,24 @@ __global__ void __launch_bounds__(kAttnMaxT)
             for (int d = 0; d < D; ++d) acc[d] = fmaf(e, vj[d], acc[d]);
         }
     }
-    const float r = inv_keep / l;
+    // combine the group's running sums at the group's maximum (lane 0 always
+    // saw key 0, so the maximum is finite; lanes without keys add zero)
+    const unsigned lanes = warp_lanes();
+    const float mg = group_max<S>(m, lanes);
+    const float c = m == -INFINITY ? 0.f : expf(m - mg);
+    l = group_sum<S>(l * c, lanes);
 #pragma unroll
-    for (int d = 0; d < D; ++d) o[base + (int64_t)i * HD + d] = acc[d] * r;
-    lse[(int64_t)(b * H + h) * T + i] = m + logf(l);
+    for (int d = 0; d < D; ++d) acc[d] = group_sum<S>(acc[d] * c, lanes);
+    if (r == 0) {
+        const float rr = inv_keep / l;
+#pragma unroll
+        for (int d = 0; d < D; ++d) o[base + (int64_t)i * HD + d] = acc[d] * rr;
+        lse[(int64_t)(b * H + h) * T + i] = mg + logf(l);
+    }
 }
 
-// grid (H, B), block T threads; dynamic shared memory (4*T*D + 2*T) floats
-template <int D>
+// grid (H, B), block T*S threads; dynamic shared memory (4*T*D + 2*T) floats
+template <int D, int S>
 __global__ void __launch_bounds__(attn_max_t(D))
     attn_bwd_kernel(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
                     const float* __restrict__ o, const float* __restrict__ dout, const float* __restrict__ lse,
@@ -127,7 +162,8 @@ __global__ void __launch_bounds__(attn_max_t(D))
     float* dos = vs + T * D;
     float* ls = dos + T * D;
     float* dsum = ls + T;
-    const int h = blockIdx.x, b = blockIdx.y, t0 = threadIdx.x;
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int t0 = (int)threadIdx.x / S, r = (int)threadIdx.x % S;
     const int HD = H * D;
     const int64_t base = (int64_t)b * T * HD + (int64_t)h * D;
     for (int e = threadIdx.x; e < T * D; e += blockDim.x) {
@@ -138,20 +174,20 @@ __global__ void __launch_bounds__(attn_max_t(D))
         vs[e] = v[at];
         dos[e] = dout[at];
     }
-    {
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
         float s = 0.f;
 #pragma unroll
         for (int d = 0; d < D; ++d) {
-            const int64_t at = base + (int64_t)t0 * HD + d;
+            const int64_t at = base + (int64_t)t * HD + d;
             s = fmaf(dout[at], o[at], s);
         }
-        dsum[t0] = s;
-        ls[t0] = lse[(int64_t)(b * H + h) * T + t0];
+        dsum[t] = s;
+        ls[t] = lse[(int64_t)(b * H + h) * T + t];
     }
     __syncthreads();
     const uint64_t seed = thr ? *seedp : 0ull;
     const uint64_t bh = (uint64_t)(b * H + h) * (uint64_t)T;
-    // dq: this thread's query i = t0, keys j <= i
+    // dq: this group's query i = t0, keys j <= i (every S-th from r)
     {
         const int i = t0;
         float qi[D], doi[D], g[D];
@@ -161,7 +197,7 @@ __global__ void __launch_bounds__(attn_max_t(D))
         for (int d = 0; d < D; ++d) g[d] = 0.f;
         const float li = ls[i], di = dsum[i];
         const uint64_t row = (bh + (uint64_t)i) * (uint64_t)T;
-        for (int j = 0; j <= i; ++j) {
+        for (int j = r; j <= i; j += S) {
             float kj[D], vj[D];
             attn_load_row<D>(ks + j * D, kj);
             attn_load_row<D>(vs + j * D, vj);
@@ -173,9 +209,13 @@ __global__ void __launch_bounds__(attn_max_t(D))
             for (int d = 0; d < D; ++d) g[d] = fmaf(ds, kj[d], g[d]);
         }
 #pragma unroll
-        for (int d = 0; d < D; ++d) dq[base + (int64_t)i * HD + d] = g[d] * scale;
+        for (int d = 0; d < D; ++d) g[d] = group_sum<S>(g[d], warp_lanes());
+        if (r == 0) {
+#pragma unroll
+            for (int d = 0; d < D; ++d) dq[base + (int64_t)i * HD + d] = g[d] * scale;
+        }
     }
-    // dk, dv: this thread's key j = t0, queries i >= j
+    // dk, dv: this group's key j = t0, queries i >= j (every S-th from j + r)
     {
         const int j = t0;
         float kj[D], vj[D], gk[D], gv[D];
@@ -183,7 +223,7 @@ __global__ void __launch_bounds__(attn_max_t(D))
         attn_load_row<D>(vs + j * D, vj);
 #pragma unroll
         for (int d = 0; d < D; ++d) gk[d] = gv[d] = 0.f;
-        for (int i = j; i < T; ++i) {
+        for (int i = j + r; i < T; i += S) {
             float qi[D], doi[D];
             attn_load_row<D>(qs + i * D, qi);
             attn_load_row<D>(dos + i * D, doi);
@@ -198,13 +238,24 @@ __global__ void __launch_bounds__(attn_max_t(D))
                 gk[d] = fmaf(ds, qi[d], gk[d]);
             }
         }
+        const unsigned lanes = warp_lanes();
 #pragma unroll
         for (int d = 0; d < D; ++d) {
-            dk[base + (int64_t)j * HD + d] = gk[d] * scale;
-            dv[base + (int64_t)j * HD + d] = gv[d];
+            gk[d] = group_sum<S>(gk[d], lanes);
+            gv[d] = group_sum<S>(gv[d], lanes);
+        }
+        if (r == 0) {
+#pragma unroll
+            for (int d = 0; d < D; ++d) {
+                dk[base + (int64_t)j * HD + d] = gk[d] * scale;
+                dv[base + (int64_t)j * HD + d] = gv[d];
+            }
         }
     }
 }
+
+// lanes per query (or key): as many as a CTA of at most `cap` threads allows, up to 4
+inline int attn_lanes(int T, int cap) { return T * 4 <= cap ? 4 : (T * 2 <= cap ? 2 : 1); }
 
 // keep[b, h, i, j] (1 = kept) of the dropout mask, for the tests
 __global__ void attn_mask_kernel(uint8_t* keep, int64_t n, int T, uint32_t thr, const uint64_t* seedp) {

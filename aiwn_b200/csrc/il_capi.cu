@@ -378,12 +378,19 @@ int il_attention_forward(const float* q, const float* k, const float* v, float* 
     const int64_t smem = il::attn_fwd_smem((int)T, (int)D);
     const int t = (int)T, h = (int)H;
     const float sc = (float)scale;
+    const int S = il::attn_lanes(t, il::kAttnMaxT);
+    const int64_t nt = T * S;
+#define IL_ATTN_FWD(DD, SS)                                                                                      \
+    attn_launch(il::attn_fwd_kernel<DD, SS>, smem, B, nt, H, s, q, k, v, o, lse, t, h, sc, thr, inv_keep, seed)
+#define IL_ATTN_FWD_S(DD) (S == 4 ? IL_ATTN_FWD(DD, 4) : S == 2 ? IL_ATTN_FWD(DD, 2) : IL_ATTN_FWD(DD, 1))
     switch (D) {
-        case 2: return attn_launch(il::attn_fwd_kernel<2>, smem, B, T, H, s, q, k, v, o, lse, t, h, sc, thr, inv_keep, seed);
-        case 4: return attn_launch(il::attn_fwd_kernel<4>, smem, B, T, H, s, q, k, v, o, lse, t, h, sc, thr, inv_keep, seed);
-        case 8: return attn_launch(il::attn_fwd_kernel<8>, smem, B, T, H, s, q, k, v, o, lse, t, h, sc, thr, inv_keep, seed);
-        default: return attn_launch(il::attn_fwd_kernel<16>, smem, B, T, H, s, q, k, v, o, lse, t, h, sc, thr, inv_keep, seed);
+        case 2: return IL_ATTN_FWD_S(2);
+        case 4: return IL_ATTN_FWD_S(4);
+        case 8: return IL_ATTN_FWD_S(8);
+        default: return IL_ATTN_FWD_S(16);
     }
+#undef IL_ATTN_FWD_S
+#undef IL_ATTN_FWD
 }
 
 int il_attention_backward(const float* q, const float* k, const float* v, const float* o, const float* dout,
@@ -400,12 +407,20 @@ int il_attention_backward(const float* q, const float* k, const float* v, const 
     const int64_t smem = il::attn_bwd_smem((int)T, (int)D);
     const int t = (int)T, h = (int)H;
     const float sc = (float)scale;
+    const int S = il::attn_lanes(t, il::attn_max_t((int)D));
+    const int64_t nt = T * S;
+#define IL_ATTN_BWD(DD, SS)                                                                                    \
+    attn_launch(il::attn_bwd_kernel<DD, SS>, smem, B, nt, H, s, q, k, v, o, dout, lse, dq, dk, dv, t, h, sc, thr, \
+                inv_keep, seed)
+#define IL_ATTN_BWD_S(DD) (S == 4 ? IL_ATTN_BWD(DD, 4) : S == 2 ? IL_ATTN_BWD(DD, 2) : IL_ATTN_BWD(DD, 1))
     switch (D) {
-        case 2: return attn_launch(il::attn_bwd_kernel<2>, smem, B, T, H, s, q, k, v, o, dout, lse, dq, dk, dv, t, h, sc, thr, inv_keep, seed);
-        case 4: return attn_launch(il::attn_bwd_kernel<4>, smem, B, T, H, s, q, k, v, o, dout, lse, dq, dk, dv, t, h, sc, thr, inv_keep, seed);
-        case 8: return attn_launch(il::attn_bwd_kernel<8>, smem, B, T, H, s, q, k, v, o, dout, lse, dq, dk, dv, t, h, sc, thr, inv_keep, seed);
-        default: return attn_launch(il::attn_bwd_kernel<16>, smem, B, T, H, s, q, k, v, o, dout, lse, dq, dk, dv, t, h, sc, thr, inv_keep, seed);
+        case 2: return IL_ATTN_BWD_S(2);
+        case 4: return IL_ATTN_BWD_S(4);
+        case 8: return IL_ATTN_BWD_S(8);
+        default: return IL_ATTN_BWD_S(16);
     }
+#undef IL_ATTN_BWD_S
+#undef IL_ATTN_BWD
 }
 
 int il_attention_dropout_mask(uint8_t* keep, int64_t B, int64_t T, int64_t H, double p, const uint64_t* seed,
