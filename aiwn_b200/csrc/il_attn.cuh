@@ -16,10 +16,10 @@
 //   so every backward lane group runs i+1 + T-i iterations.
 //
 // q, k, v, o, dq, dk, dv are [B, T, H*D] (the projections' own layout: no
-// head transposes).  Dropout keeps element (b, h, i, j) when the top 32 bits
-// of splitmix64 (Steele, Lea and Flood, 2014) of seed + index * golden-ratio
-// constant reach p * 2^32; the backward regenerates the same mask from the
-// same device-resident seed.
+// head transposes).  Dropout keeps element (b, h, i, j) when a 32-bit hash
+// (MurmurHash3's finaliser) of the score row's key plus j reaches p * 2^32;
+// the row key mixes the device-resident 64-bit seed with the row index, so
+// the backward regenerates the same mask from the same seed.
 #pragma once
 #include <cuda_runtime.h>
 #include <math.h>
@@ -31,12 +31,25 @@ constexpr int kAttnMaxT = 1024;
 // the 16-feature backward keeps more state per thread: at most 512 positions
 __host__ __device__ constexpr int attn_max_t(int D) { return D >= 16 ? 512 : kAttnMaxT; }
 
-__device__ __forceinline__ bool attn_keep(uint64_t seed, uint64_t idx, uint32_t thr) {
-    uint64_t z = seed + idx * 0x9E3779B97F4A7C15ull;
-    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-    z ^= z >> 31;
-    return (uint32_t)(z >> 32) >= thr;
+// MurmurHash3's 32-bit finaliser (Appleby, public domain)
+__device__ __forceinline__ uint32_t fmix32(uint32_t h) {
+    h ^= h >> 16;
+    h *= 0x85EBCA6Bu;
+    h ^= h >> 13;
+    h *= 0xC2B2AE35u;
+    h ^= h >> 16;
+    return h;
+}
+
+// the key of score row (b*H + h)*T + i under a 64-bit seed
+__device__ __forceinline__ uint32_t attn_row_key(uint64_t seed, uint64_t row) {
+    const uint32_t mixed = (uint32_t)(seed >> 32) + (uint32_t)row * 0x9E3779B9u + (uint32_t)(row >> 32);
+    return fmix32((uint32_t)seed ^ fmix32(mixed));
+}
+
+// element (row, j) is kept when fmix32(row key + j * 0x85EBCA77) >= p * 2^32
+__device__ __forceinline__ bool attn_keep(uint32_t row_key, int j, uint32_t thr) {
+    return fmix32(row_key + (uint32_t)j * 0x85EBCA77u) >= thr;
 }
 
 template <int D>
@@ -112,7 +125,7 @@ __global__ void __launch_bounds__(kAttnMaxT)
         acc[d] = 0.f;
     }
     float m = -INFINITY, l = 0.f;
-    const uint64_t row = ((uint64_t)(b * H + h) * (uint64_t)T + (uint64_t)i) * (uint64_t)T;
+    const uint32_t rk = thr ? attn_row_key(seed, (uint64_t)(b * H + h) * (uint64_t)T + (uint64_t)i) : 0u;
     for (int j = r; j <= i; j += S) {
         float kj[D], vj[D];
         attn_load_row<D>(ks + j * D, kj);
@@ -126,7 +139,7 @@ __global__ void __launch_bounds__(kAttnMaxT)
         }
         const float e = expf(s - m);
         l += e;
-        if (thr == 0u || attn_keep(seed, row + (uint64_t)j, thr)) {
+        if (thr == 0u || attn_keep(rk, j, thr)) {
             attn_load_row<D>(vs + j * D, vj);
 #pragma unroll
             for (int d = 0; d < D; ++d) acc[d] = fmaf(e, vj[d], acc[d]);
@@ -162,6 +175,7 @@ __global__ void __launch_bounds__(attn_max_t(D))
     float* dos = vs + T * D;
     float* ls = dos + T * D;
     float* dsum = ls + T;
+    uint32_t* rks = reinterpret_cast<uint32_t*>(dsum + T);  // row keys of the dropout mask
     const int h = blockIdx.x, b = blockIdx.y;
     const int t0 = (int)threadIdx.x / S, r = (int)threadIdx.x % S;
     const int HD = H * D;
@@ -183,10 +197,9 @@ __global__ void __launch_bounds__(attn_max_t(D))
         }
         dsum[t] = s;
         ls[t] = lse[(int64_t)(b * H + h) * T + t];
+        rks[t] = thr ? attn_row_key(*seedp, (uint64_t)(b * H + h) * (uint64_t)T + (uint64_t)t) : 0u;
     }
     __syncthreads();
-    const uint64_t seed = thr ? *seedp : 0ull;
-    const uint64_t bh = (uint64_t)(b * H + h) * (uint64_t)T;
     // dq: this group's query i = t0, keys j <= i (every S-th from r)
     {
         const int i = t0;
@@ -196,13 +209,13 @@ __global__ void __launch_bounds__(attn_max_t(D))
 #pragma unroll
         for (int d = 0; d < D; ++d) g[d] = 0.f;
         const float li = ls[i], di = dsum[i];
-        const uint64_t row = (bh + (uint64_t)i) * (uint64_t)T;
+        const uint32_t rk = rks[i];
         for (int j = r; j <= i; j += S) {
             float kj[D], vj[D];
             attn_load_row<D>(ks + j * D, kj);
             attn_load_row<D>(vs + j * D, vj);
             const float p = expf(attn_dot<D>(qi, kj) * scale - li);
-            const bool keep = thr == 0u || attn_keep(seed, row + (uint64_t)j, thr);
+            const bool keep = thr == 0u || attn_keep(rk, j, thr);
             const float dp = keep ? attn_dot<D>(doi, vj) * inv_keep : 0.f;
             const float ds = p * (dp - di);
 #pragma unroll
@@ -228,7 +241,7 @@ __global__ void __launch_bounds__(attn_max_t(D))
             attn_load_row<D>(qs + i * D, qi);
             attn_load_row<D>(dos + i * D, doi);
             const float p = expf(attn_dot<D>(qi, kj) * scale - ls[i]);
-            const bool keep = thr == 0u || attn_keep(seed, (bh + (uint64_t)i) * (uint64_t)T + (uint64_t)j, thr);
+            const bool keep = thr == 0u || attn_keep(rks[i], j, thr);
             const float z = keep ? p * inv_keep : 0.f;
             const float dp = keep ? attn_dot<D>(doi, vj) * inv_keep : 0.f;
             const float ds = p * (dp - dsum[i]);
@@ -261,11 +274,10 @@ inline int attn_lanes(int T, int cap) { return T * 4 <= cap ? 4 : (T * 2 <= cap 
 __global__ void attn_mask_kernel(uint8_t* keep, int64_t n, int T, uint32_t thr, const uint64_t* seedp) {
     const uint64_t seed = *seedp;
     for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x)
-        keep[e] = attn_keep(seed, (uint64_t)e, thr) ? 1 : 0;
-    (void)T;
+        keep[e] = attn_keep(attn_row_key(seed, (uint64_t)(e / T)), (int)(e % T), thr) ? 1 : 0;
 }
 
 inline int64_t attn_fwd_smem(int T, int D) { return (int64_t)2 * T * D * 4; }
-inline int64_t attn_bwd_smem(int T, int D) { return ((int64_t)4 * T * D + 2 * T) * 4; }
+inline int64_t attn_bwd_smem(int T, int D) { return ((int64_t)4 * T * D + 3 * T) * 4; }
 
 }  // namespace il

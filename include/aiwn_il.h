@@ -175,8 +175,10 @@ IL_API int il_layernorm_backward(const float* gy, const float* x, const float* g
  * [B, T, H*D] (head h in columns h*D..h*D+D-1); lse [B, H, T] receives the
  * log-sum-exp of each query's scores for the backward.  With p > 0, *seed
  * (device memory) selects the dropout mask; the backward must get the same
- * seed.  Element (b, h, i, j) is kept when the top 32 bits of splitmix64 of
- * seed + index * 0x9E3779B97F4A7C15 are >= p * 2^32 (index = ((b*H+h)*T+i)*T+j).
+ * seed.  Element (b, h, i, j) is kept when fmix32(rk + j * 0x85EBCA77) >= p *
+ * 2^32, with fmix32 MurmurHash3's 32-bit finaliser and the row key
+ * rk = fmix32(lo32(seed) ^ fmix32(hi32(seed) + lo32(row) * 0x9E3779B9 + hi32(row))),
+ * row = (b*H + h)*T + i.
  */
 IL_API int il_attention_forward(const float* q, const float* k, const float* v, float* o, float* lse, int64_t B,
                          int64_t T, int64_t H, int64_t D, double scale, double p, const uint64_t* seed,

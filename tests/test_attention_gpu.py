@@ -61,7 +61,12 @@ def test_attention_matches_explicit(shape, p):
     torch.cuda.synchronize()
     normwise_close(oa.detach().cpu().numpy(), orf.detach().cpu().numpy(), FWD_RTOL, "o")
     for name, a, r in (("dq", qa, qr), ("dk", ka, kr), ("dv", va, vr)):
-        normwise_close(a.grad.cpu().numpy(), r.grad.cpu().numpy(), GRAD_RTOL, name)
+        got, ref = a.grad.cpu().numpy(), r.grad.cpu().numpy()
+        if not ref.any():
+            # zero in exact arithmetic (e.g. dq over a single position): rounding noise only
+            assert abs(got).max() < 1e-6, name
+            continue
+        normwise_close(got, ref, GRAD_RTOL, name)
 
 
 def test_dropout_masks_differ_by_seed_and_repeat_for_a_seed():
