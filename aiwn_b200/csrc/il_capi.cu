@@ -169,6 +169,16 @@ int forward_dispatch(const void* x, int x_dtype, const float* table, const float
     return launch_status();
 }
 
+// zeroes a[0..na) and b[0..nb) (either may be NULL) with one memset when b
+// directly follows a in memory, as the library's own callers allocate them
+int zero_pair(float* a, int64_t na, float* b, int64_t nb, cudaStream_t s) {
+    if (a && b && b == a + na)
+        return cudaMemsetAsync(a, 0, (size_t)(na + nb) * sizeof(float), s) == cudaSuccess ? IL_OK : IL_ERR_LAUNCH;
+    if (a && cudaMemsetAsync(a, 0, (size_t)na * sizeof(float), s) != cudaSuccess) return IL_ERR_LAUNCH;
+    if (b && cudaMemsetAsync(b, 0, (size_t)nb * sizeof(float), s) != cudaSuccess) return IL_ERR_LAUNCH;
+    return IL_OK;
+}
+
 // shape, dropout and seed checks shared by the attention entry points
 int attn_check(int64_t B, int64_t T, int64_t H, int64_t D, double p, const uint64_t* seed, bool bwd) {
     if (B < 1 || B > 65535 || H < 1 || H > 65535 || T < 1 || T > il::kAttnMaxT) return IL_ERR_SHAPE;
@@ -282,8 +292,7 @@ int il_cdf_backward(const float* gxn, const float* x, const float* gamma, const 
     int st = check_device(&sms);
     if (st) return st;
     cudaStream_t s = (cudaStream_t)stream;
-    if (dgamma && cudaMemsetAsync(dgamma, 0, (size_t)IN * sizeof(float), s) != cudaSuccess) return IL_ERR_LAUNCH;
-    if (dbeta && cudaMemsetAsync(dbeta, 0, (size_t)IN * sizeof(float), s) != cudaSuccess) return IL_ERR_LAUNCH;
+    if ((st = zero_pair(dgamma, IN, dbeta, IN, s))) return st;
     if (N == 0 || (!dx && !dgamma && !dbeta)) return IL_OK;
     if (IN <= il::kCdfMaxIn) {
         const int vec = (IN % 4 == 0) && ((((uintptr_t)gxn | (uintptr_t)x | (uintptr_t)dx) & 15) == 0);
@@ -346,8 +355,7 @@ int il_layernorm_backward(const float* gy, const float* x, const float* gamma, c
     int st = check_device(&sms);
     if (st) return st;
     cudaStream_t s = (cudaStream_t)stream;
-    if (dgamma && cudaMemsetAsync(dgamma, 0, (size_t)IN * sizeof(float), s) != cudaSuccess) return IL_ERR_LAUNCH;
-    if (dbeta && cudaMemsetAsync(dbeta, 0, (size_t)IN * sizeof(float), s) != cudaSuccess) return IL_ERR_LAUNCH;
+    if ((st = zero_pair(dgamma, IN, dbeta, IN, s))) return st;
     if (N == 0 || (!dx && !dgamma && !dbeta)) return IL_OK;
     const int vec = (IN % 4 == 0) && ((((uintptr_t)gy | (uintptr_t)x | (uintptr_t)dx) & 15) == 0);
     // one wave, several tokens per thread: the block reduction runs once per block
@@ -456,10 +464,7 @@ static int backward_impl(const float* go, const void* x, int x_dtype, const floa
     const il::BinCfg c = make_cfg(bw, K);
     const int64_t need = il::fast_backward_workspace(N, IN, OUT, K, x_dtype);
     if (need > 0 && (!workspace || workspace_bytes < need)) return IL_ERR_WORKSPACE;
-    if (!accumulate && gt && cudaMemsetAsync(gt, 0, (size_t)(K * IN * OUT) * sizeof(float), s) != cudaSuccess)
-        return IL_ERR_LAUNCH;
-    if (!accumulate && gb && cudaMemsetAsync(gb, 0, (size_t)OUT * sizeof(float), s) != cudaSuccess)
-        return IL_ERR_LAUNCH;
+    if (!accumulate && (st = zero_pair(gt, K * IN * OUT, gb, OUT, s))) return st;
     if (N == 0) return IL_OK;
     const KernelChoice path = kernel_choice("AIWN_IL_BACKWARD", "sorted", "gather");
     if (path != kOnlyOther &&

@@ -27,7 +27,7 @@ import torch.nn.functional as F
 
 from . import _lib
 from .layers import GaussianCDFNorm, IndexedLinear
-from .layers.indexed_linear import TRITON_OK
+from .layers.indexed_linear import TRITON_OK, grad_pair
 from .layers.indexed_linear_v2 import _FnV2
 
 
@@ -52,8 +52,8 @@ class _LayerNormFn(torch.autograd.Function):
         x2, weight, mean, rstd = ctx.saved_tensors
         gy2 = gy.reshape(x2.shape).contiguous()
         dx = torch.empty_like(x2) if ctx.needs_input_grad[0] else None
-        dw = torch.empty_like(weight) if ctx.needs_input_grad[1] else None
-        db = torch.empty_like(weight) if ctx.needs_input_grad[2] else None
+        dw, db = grad_pair(weight.shape, weight.shape, weight.device, ctx.needs_input_grad[1],
+                           ctx.needs_input_grad[2])
         _lib.layernorm_backward(gy2, x2, weight, mean, rstd, dx, dw, db)
         return (dx.reshape(ctx.shape) if dx is not None else None), dw, db, None
 

@@ -55,8 +55,7 @@ class _Fn(torch.autograd.Function):
             go = go.float()
         need_x, need_t, need_b = ctx.needs_input_grad[:3]
         gx = torch.empty_like(x) if need_x else None
-        gt = torch.empty_like(tab) if need_t else None
-        gb = torch.empty(tab.shape[2], dtype=torch.float32, device=x.device) if need_b else None
+        gt, gb = grad_pair(tab.shape, (tab.shape[2],), x.device, need_t, need_b)
         if gx is None and gt is None and gb is None:
             return None, None, None, None
         N, IN = x.shape
@@ -65,6 +64,19 @@ class _Fn(torch.autograd.Function):
         ws = torch.empty(ws_n, dtype=torch.uint8, device=x.device) if ws_n > 0 else None
         _lib.backward(go, x, tab, gx, gt, gb, ctx.bw, ws)
         return gx, gt, gb, None
+
+
+def grad_pair(shape_a, shape_b, device, need_a: bool, need_b: bool):
+    """Two fp32 gradient outputs (None where not needed).  When both are
+    needed they share one allocation with b right after a, so the library
+    zeroes them with one memset instead of two."""
+    na, nb = math.prod(shape_a), math.prod(shape_b)
+    if need_a and need_b:
+        buf = torch.empty(na + nb, dtype=torch.float32, device=device)
+        return buf[:na].view(shape_a), buf[na:].view(shape_b)
+    a = torch.empty(shape_a, dtype=torch.float32, device=device) if need_a else None
+    b = torch.empty(shape_b, dtype=torch.float32, device=device) if need_b else None
+    return a, b
 
 
 class IndexedLinear(nn.Module):

@@ -31,7 +31,7 @@ import torch
 import torch.nn as nn
 
 from .. import _lib
-from .indexed_linear import TRITON_OK, IndexedLinear
+from .indexed_linear import TRITON_OK, IndexedLinear, grad_pair
 
 
 class GaussianCDFNorm(nn.Module):
@@ -73,13 +73,11 @@ class _FnV2(torch.autograd.Function):
         need_x, need_g, need_b, _, need_t, need_bias = ctx.needs_input_grad[:6]
         need_pro = need_x or need_g or need_b
         gxn = torch.empty_like(xn) if need_pro else None
-        gt = torch.empty_like(tab) if need_t else None
-        gbias = torch.empty(tab.shape[2], dtype=torch.float32, device=x.device) if need_bias else None
+        gt, gbias = grad_pair(tab.shape, (tab.shape[2],), x.device, need_t, need_bias)
         if gxn is not None or gt is not None or gbias is not None:
             _lib.backward(go, xn, tab, gxn, gt, gbias, ctx.bw)
         dx = torch.empty_like(x) if need_x else None
-        dgamma = torch.empty_like(gamma) if need_g else None
-        dbeta = torch.empty_like(beta) if need_b else None
+        dgamma, dbeta = grad_pair(gamma.shape, beta.shape, x.device, need_g, need_b)
         if need_pro:
             _lib.cdf_backward(gxn, x, gamma, beta, mean, rstd, dx, dgamma, dbeta)
         return dx, dgamma, dbeta, None, gt, gbias, None
