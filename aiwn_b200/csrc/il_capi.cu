@@ -109,13 +109,15 @@ inline unsigned grid_for(int64_t work, int threads, int num_sms) {
 int forward_dispatch(const void* x, int x_dtype, const float* table, const float* bias, float* out, int64_t N,
                      int64_t IN, int64_t OUT, const il::BinCfg& c, int sms, cudaStream_t s) {
     const KernelChoice path = kernel_choice("AIWN_IL_FORWARD", "token", "cluster");
-    // Rows of a multiple of 32 outputs, where the token kernel would use its
-    // widest j-ranges: the cluster kernel's lanes read consecutive chunks of
-    // one table row, and it beat the token kernel's per-lane gathers at
-    // 32x32, 64x64 and 128x128 for N = 2 K .. 131 K tokens (e.g. 64x64, K=16:
-    // 13.8 against 23.7 us at 2 K tokens, 218 against 275 us at 131 K).
-    // Tables without a token plan keep the streamed kernel.
-    if (path == kAny && OUT % 32 == 0 &&
+    // Rows of a multiple of 32 outputs over few bins (K <= 64): the cluster
+    // kernel's lanes read consecutive chunks of one table row, and it beat the
+    // token kernel's per-lane gathers at 32x32 (K=64), 64x64 and 128x128
+    // (K=16) for N = 2 K .. 131 K tokens (e.g. 64x64, K=16: 13.8 against
+    // 23.7 us at 2 K tokens, 218 against 275 us at 131 K).  With more bins the
+    // token kernel stays ahead (20x64, K=512: 126 against 224 us; 32x64,
+    // K=128: 205 against 228 us at 131 K).  Tables without a token plan keep
+    // the streamed kernel.
+    if (path == kAny && OUT % 32 == 0 && c.K <= 64 &&
         il::fast_forward_args_ok(x, x_dtype, table, bias, out, N, IN, OUT, c.K, c)) {
         il::FwdPlan pl;
         if (il::plan_token_forward(N, c.K, (int)IN, (int)OUT, sms, pl) &&

@@ -61,7 +61,7 @@ def check_against_oracle(c, x, table, bias, go):
 @pytest.mark.parametrize("c", CASES + EDGE_CASES, ids=lambda c: c.name)
 def test_parity_vs_oracle(c, paths, monkeypatch):
     """auto: the library's own choice (cluster forward for rows of >= 32
-    outputs, else one token per lane; bin-sorted backward) wherever there is a
+    outputs at K <= 64, else one token per lane; bin-sorted backward) wherever there is a
     plan; pinned: the token forward and the sorted backward wherever they have
     a plan; alt: the cluster forward and the gather backward with per-token
     table-gradient reductions."""
