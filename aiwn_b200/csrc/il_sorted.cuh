@@ -328,7 +328,7 @@ struct SrtPlan {
     int C = 0, TT = 0, R = 0, tok_per_cta = 0, smem = 0, jranges = 1;
 };
 
-constexpr int kSrtChunks[] = {32, 20, 16, 10, 8, 5, 4, 2, 1};
+constexpr int kSrtChunks[] = {32, 20, 16, 12, 10, 8, 5, 4, 2, 1};
 
 // j-ranges of 4*C output columns: one range when OUT/4 is an instantiated C,
 // else equal ranges of the widest power-of-two C <= 32 dividing OUT/4
@@ -382,6 +382,7 @@ inline int launch_sorted_c(const SrtArgs& a, const SrtPlan& pl, cudaStream_t s) 
         case 32: return launch_sorted<DT, 32>(a, pl, s);
         case 20: return launch_sorted<DT, 20>(a, pl, s);
         case 16: return launch_sorted<DT, 16>(a, pl, s);
+        case 12: return launch_sorted<DT, 12>(a, pl, s);
         case 10: return launch_sorted<DT, 10>(a, pl, s);
         case 8: return launch_sorted<DT, 8>(a, pl, s);
         case 5: return launch_sorted<DT, 5>(a, pl, s);

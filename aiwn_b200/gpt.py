@@ -27,7 +27,7 @@ import torch.nn.functional as F
 
 from . import _lib
 from .layers import GaussianCDFNorm, IndexedLinear
-from .layers.indexed_linear import TRITON_OK, grad_pair
+from .layers.indexed_linear import TRITON_OK, _Fn, grad_pair
 from .layers.indexed_linear_v2 import _FnV2
 
 
@@ -137,12 +137,25 @@ class IndexedAttention(nn.Module):
         self.register_buffer("bias", torch.tril(torch.ones(block_size, block_size)).view(1, 1, block_size,
                                                                                           block_size))
 
+    def _qkv(self, h, B, T):
+        """q, k, v [B, T, d_idx].  With the fused form and no hooks on the
+        projections, one IndexedLinear over the three tables concatenated along
+        out_d computes [q | k | v] (each output column depends only on its own
+        table column, and dx sums over all of them): one forward and one
+        backward instead of three of each."""
+        projs = (self.q_proj, self.k_proj, self.v_proj)
+        if (self.fused and h.is_cuda and h.dtype == torch.float32 and TRITON_OK
+                and not any(m._forward_pre_hooks or m._forward_hooks for m in projs)):
+            tab = torch.cat([m.table for m in projs], dim=2)
+            bias = torch.cat([m.bias for m in projs])
+            qkv = _Fn.apply(h.contiguous(), tab, bias, self.q_proj.bw).view(B, T, 3 * self.d_idx)
+            return qkv.split(self.d_idx, dim=2)
+        return tuple(m(h).reshape(B, T, self.d_idx) for m in projs)
+
     def forward(self, x):
         B, T, C = x.shape
         h = x.reshape(B * T, C)
-        q = self.q_proj(h).reshape(B, T, self.d_idx)
-        k = self.k_proj(h).reshape(B, T, self.d_idx)
-        v = self.v_proj(h).reshape(B, T, self.d_idx)
+        q, k, v = self._qkv(h, B, T)
         D = C // self.n_head
         if self.fused and q.is_cuda and q.dtype == torch.float32 and _lib.attention_supported(T, D):
             p = self.attn_drop.p if self.training else 0.0

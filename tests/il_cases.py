@@ -51,6 +51,9 @@ EDGE_CASES = [
     Case("out256_k32_jranges", 700, 6, 256, 32, "wide", "f32", 0.3, 30),
     Case("out256_k64_bf16", 500, 8, 256, 64, "wide", "bf16", 0.3, 31),
     Case("out176_k32_jranges", 500, 12, 176, 32, "wide", "f32", 0.3, 34),  # 11 j-ranges of 16 columns
+    # out_d 48: the sorted backward's 12-lane groups (IndexedGPT's fused q|k|v projection)
+    Case("out48_k128_qkv", 3000, 16, 48, 128, "wide", "f32", 0.3, 36),
+    Case("out48_k128_qkv_bf16", 3000, 16, 48, 128, "wide", "bf16", 0.3, 37),
     # too large to keep resident: the streamed forward (partial last column chunk, partial token tile)
     Case("stream_in300_out8_k256", 600, 300, 8, 256, "wide", "f32", 0.3, 32),
     Case("stream_in300_out8_k256_bf16", 600, 300, 8, 256, "wide", "bf16", 0.3, 33),
