@@ -134,6 +134,39 @@ class _on_device:
             torch.cuda.set_device(self.prev)
 
 
+def _expect(name: str, t, shape, dtype=torch.float32):
+    """Raise ILError unless tensor `t` (skipped when None) has exactly this
+    dtype and shape: the C entry points trust every size they are given, so a
+    mismatch caught here is one that never reaches a kernel."""
+    if t is None:
+        return
+    if t.dtype != dtype:
+        raise ILError(f"{name}: dtype {t.dtype}, expected {dtype}")
+    if tuple(t.shape) != tuple(shape):
+        raise ILError(f"{name}: shape {tuple(t.shape)}, expected {tuple(shape)}")
+
+
+def _same_device(*ts):
+    devs = {t.device for t in ts if t is not None}
+    if len(devs) > 1:
+        raise ILError(f"tensors on different devices: {sorted(str(d) for d in devs)}")
+
+
+def _layer_shapes(x, table):
+    """(N, IN, OUT, K) of an IndexedLinear call, checking x [N, IN] against
+    table [K, IN, OUT]."""
+    if x.dim() != 2:
+        raise ILError(f"x must be [N, in_d], got shape {tuple(x.shape)}")
+    if table.dim() != 3:
+        raise ILError(f"table must be [K, in_d, out_d], got shape {tuple(table.shape)}")
+    N, IN = x.shape
+    K, tin, OUT = table.shape
+    if tin != IN:
+        raise ILError(f"x has in_d {IN} but the table has {tin}")
+    _expect("table", table, (K, IN, OUT))
+    return N, IN, OUT, K
+
+
 def x_dtype_code(x: torch.Tensor) -> int:
     try:
         return _DTYPES[x.dtype]
@@ -143,9 +176,12 @@ def x_dtype_code(x: torch.Tensor) -> int:
 
 def forward(x, table, bias, out, bw: float):
     """out[N, OUT] (fp32) <- IndexedLinear forward of x[N, IN]."""
+    _same_device(x, table, bias, out)
+    N, IN, OUT, K = _layer_shapes(x, table)
+    x_dtype_code(x)
+    _expect("bias", bias, (OUT,))
+    _expect("out", out, (N, OUT))
     _need_cuda(x, table, bias, out)
-    N, IN = x.shape
-    K, _, OUT = table.shape
     lib = load()
     with _on_device(x.device):
         _check(lib.il_forward(_p(x), x_dtype_code(x), _p(table), _p(bias), _p(out),
@@ -160,9 +196,18 @@ def workspace_bytes(N, IN, OUT, K, x_dtype: int) -> int:
 def backward(go, x, table, gx, gt, gb, bw: float, workspace=None, accumulate: bool = False):
     """gx / gt / gb (any may be None) <- gradients of the forward; with
     ``accumulate`` gt and gb are added into instead of overwritten."""
+    _same_device(go, x, table, gx, gt, gb, workspace)
+    N, IN, OUT, K = _layer_shapes(x, table)
+    xdt = x_dtype_code(x)
+    _expect("go", go, (N, OUT))
+    _expect("gx", gx, (N, IN), x.dtype)
+    _expect("gt", gt, (K, IN, OUT))
+    _expect("gb", gb, (OUT,))
+    if workspace is not None and workspace.dtype != torch.uint8:
+        raise ILError("workspace must be a uint8 tensor")
+    if workspace_bytes(N, IN, OUT, K, xdt) > (0 if workspace is None else workspace.numel()):
+        raise ILError("workspace missing or smaller than workspace_bytes()")
     _need_cuda(go, x, table, gx, gt, gb, workspace)
-    N, IN = x.shape
-    K, _, OUT = table.shape
     lib = load()
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     fn, name = (lib.il_backward_accumulate, "il_backward_accumulate") if accumulate else (lib.il_backward,
@@ -175,11 +220,14 @@ def backward(go, x, table, gx, gt, gb, bw: float, workspace=None, accumulate: bo
 def cdf_forward(x, gamma, beta, eps: float, table, bias, xn, mean, rstd, out, bw: float):
     """IndexedLinearV2 forward: xn <- GaussianCDFNorm(x), out <- IndexedLinear(xn);
     also the per-token LayerNorm mean and rstd.  fp32 x [N, IN]."""
-    _need_cuda(x, gamma, beta, table, bias, xn, mean, rstd, out)
+    _same_device(x, gamma, beta, table, bias, xn, mean, rstd, out)
     if x.dtype != torch.float32:
         raise ILError("il_cdf_forward takes fp32 x")
-    N, IN = x.shape
-    K, _, OUT = table.shape
+    N, IN, OUT, K = _layer_shapes(x, table)
+    for name, t, shp in (("gamma", gamma, (IN,)), ("beta", beta, (IN,)), ("bias", bias, (OUT,)),
+                         ("xn", xn, (N, IN)), ("mean", mean, (N,)), ("rstd", rstd, (N,)), ("out", out, (N, OUT))):
+        _expect(name, t, shp)
+    _need_cuda(x, gamma, beta, table, bias, xn, mean, rstd, out)
     lib = load()
     with _on_device(x.device):
         _check(lib.il_cdf_forward(_p(x), _p(gamma), _p(beta), float(eps), _p(table), _p(bias), _p(xn), _p(mean),
@@ -190,8 +238,15 @@ def cdf_forward(x, gamma, beta, eps: float, table, bias, xn, mean, rstd, out, bw
 
 def cdf_backward(gxn, x, gamma, beta, mean, rstd, dx, dgamma, dbeta):
     """dx / dgamma / dbeta (any may be None) <- backward of the GaussianCDFNorm prologue."""
-    _need_cuda(gxn, x, gamma, beta, mean, rstd, dx, dgamma, dbeta)
+    _same_device(gxn, x, gamma, beta, mean, rstd, dx, dgamma, dbeta)
+    if x.dim() != 2:
+        raise ILError(f"x must be [N, in_d], got shape {tuple(x.shape)}")
     N, IN = x.shape
+    for name, t, shp in (("gxn", gxn, (N, IN)), ("x", x, (N, IN)), ("gamma", gamma, (IN,)), ("beta", beta, (IN,)),
+                         ("mean", mean, (N,)), ("rstd", rstd, (N,)), ("dx", dx, (N, IN)), ("dgamma", dgamma, (IN,)),
+                         ("dbeta", dbeta, (IN,))):
+        _expect(name, t, shp)
+    _need_cuda(gxn, x, gamma, beta, mean, rstd, dx, dgamma, dbeta)
     lib = load()
     with _on_device(x.device):
         _check(lib.il_cdf_backward(_p(gxn), _p(x), _p(gamma), _p(beta), _p(mean), _p(rstd), _p(dx), _p(dgamma),
@@ -201,8 +256,14 @@ def cdf_backward(gxn, x, gamma, beta, mean, rstd, dx, dgamma, dbeta):
 def layernorm_forward(x, gamma, beta, eps: float, y, mean, rstd):
     """y <- LayerNorm(x; gamma, beta, eps) over the last dim (fp32 x [N, IN],
     IN <= 32); also the per-row mean and rstd [N]."""
-    _need_cuda(x, gamma, beta, y, mean, rstd)
+    _same_device(x, gamma, beta, y, mean, rstd)
+    if x.dim() != 2:
+        raise ILError(f"x must be [N, in_d], got shape {tuple(x.shape)}")
     N, IN = x.shape
+    for name, t, shp in (("x", x, (N, IN)), ("gamma", gamma, (IN,)), ("beta", beta, (IN,)), ("y", y, (N, IN)),
+                         ("mean", mean, (N,)), ("rstd", rstd, (N,))):
+        _expect(name, t, shp)
+    _need_cuda(x, gamma, beta, y, mean, rstd)
     lib = load()
     with _on_device(x.device):
         _check(lib.il_layernorm_forward(_p(x), _p(gamma), _p(beta), float(eps), _p(y), _p(mean), _p(rstd), N, IN,
@@ -212,8 +273,14 @@ def layernorm_forward(x, gamma, beta, eps: float, y, mean, rstd):
 
 def layernorm_backward(gy, x, gamma, mean, rstd, dx, dgamma, dbeta):
     """dx / dgamma / dbeta (any may be None) <- backward of layernorm_forward."""
-    _need_cuda(gy, x, gamma, mean, rstd, dx, dgamma, dbeta)
+    _same_device(gy, x, gamma, mean, rstd, dx, dgamma, dbeta)
+    if x.dim() != 2:
+        raise ILError(f"x must be [N, in_d], got shape {tuple(x.shape)}")
     N, IN = x.shape
+    for name, t, shp in (("gy", gy, (N, IN)), ("x", x, (N, IN)), ("gamma", gamma, (IN,)), ("mean", mean, (N,)),
+                         ("rstd", rstd, (N,)), ("dx", dx, (N, IN)), ("dgamma", dgamma, (IN,)), ("dbeta", dbeta, (IN,))):
+        _expect(name, t, shp)
+    _need_cuda(gy, x, gamma, mean, rstd, dx, dgamma, dbeta)
     lib = load()
     with _on_device(x.device):
         _check(lib.il_layernorm_backward(_p(gy), _p(x), _p(gamma), _p(mean), _p(rstd), _p(dx), _p(dgamma),
@@ -225,11 +292,32 @@ def attention_supported(T: int, D: int) -> bool:
     return D in (2, 4, 8, 16) and 1 <= T <= (512 if D == 16 else 1024)
 
 
+def _attn_shapes(q, H: int):
+    if q.dim() != 3 or H < 1 or q.shape[2] % H != 0:
+        raise ILError(f"q must be [B, T, H*D] with H={H} dividing the last dimension, got {tuple(q.shape)}")
+    _expect("q", q, tuple(q.shape))
+    return q.shape
+
+
+def _expect_seed(seed, p: float):
+    if seed is None:
+        if p > 0:
+            raise ILError("dropout p > 0 needs a device seed tensor")
+        return
+    if seed.dtype not in (torch.int64, torch.uint64) or seed.numel() < 1:
+        raise ILError("seed must be an int64 device tensor of at least one element")
+
+
 def attention_forward(q, k, v, o, lse, H: int, scale: float, p: float, seed):
     """o <- causal attention of fp32 q, k, v [B, T, H*D] (dropout p, device
     int64 seed [1]); lse [B, H, T] for the backward."""
+    _same_device(q, k, v, o, lse, seed)
+    B, T, C = _attn_shapes(q, H)
+    for name, t in (("k", k), ("v", v), ("o", o)):
+        _expect(name, t, (B, T, C))
+    _expect("lse", lse, (B, H, T))
+    _expect_seed(seed, p)
     _need_cuda(q, k, v, o, lse, seed)
-    B, T, C = q.shape
     lib = load()
     with _on_device(q.device):
         _check(lib.il_attention_forward(_p(q), _p(k), _p(v), _p(o), _p(lse), B, T, H, C // H, float(scale),
@@ -239,8 +327,13 @@ def attention_forward(q, k, v, o, lse, H: int, scale: float, p: float, seed):
 
 def attention_backward(q, k, v, o, do, lse, dq, dk, dv, H: int, scale: float, p: float, seed):
     """dq, dk, dv <- backward of attention_forward given do = dL/do."""
+    _same_device(q, k, v, o, do, lse, dq, dk, dv, seed)
+    B, T, C = _attn_shapes(q, H)
+    for name, t in (("k", k), ("v", v), ("o", o), ("do", do), ("dq", dq), ("dk", dk), ("dv", dv)):
+        _expect(name, t, (B, T, C))
+    _expect("lse", lse, (B, H, T))
+    _expect_seed(seed, p)
     _need_cuda(q, k, v, o, do, lse, dq, dk, dv, seed)
-    B, T, C = q.shape
     lib = load()
     with _on_device(q.device):
         _check(lib.il_attention_backward(_p(q), _p(k), _p(v), _p(o), _p(do), _p(lse), _p(dq), _p(dk), _p(dv), B, T,
@@ -250,6 +343,9 @@ def attention_backward(q, k, v, o, do, lse, dq, dk, dv, H: int, scale: float, p:
 
 def attention_dropout_mask(keep, B: int, T: int, H: int, p: float, seed):
     """keep [B, H, T, T] uint8 <- the dropout mask attention_forward uses."""
+    _same_device(keep, seed)
+    _expect("keep", keep, (B, H, T, T), torch.uint8)
+    _expect_seed(seed, 1.0)
     _need_cuda(keep, seed)
     lib = load()
     with _on_device(keep.device):
@@ -259,9 +355,11 @@ def attention_dropout_mask(keep, B: int, T: int, H: int, p: float, seed):
 
 def bin_counts(x, K: int, bw: float, counts):
     """counts[K] (int64, device) += occupancy of the bins of x[..., IN]."""
-    _need_cuda(x, counts)
+    _same_device(x, counts)
     if counts.dtype != torch.int64 or counts.numel() != K:
         raise ILError("bin_counts needs an int64 counts tensor of K elements")
+    x_dtype_code(x)
+    _need_cuda(x, counts)
     x2 = x.reshape(-1, x.shape[-1])
     lib = load()
     with _on_device(x.device):
@@ -284,10 +382,13 @@ def bins(x, K: int, bw: float):
 
 
 def adam_step(p, g, m, v, lr, beta1, beta2, eps, step: int):
-    _need_cuda(p, g, m, v)
+    _same_device(p, g, m, v)
     for t in (p, g, m, v):
         if t.dtype != torch.float32:
             raise ILError("il_adam_step works on fp32 tensors")
+        if t.numel() != p.numel():
+            raise ILError("il_adam_step: p, g, m and v must have the same number of elements")
+    _need_cuda(p, g, m, v)
     with _on_device(p.device):
         _check(load().il_adam_step(_p(p), _p(g), _p(m), _p(v), p.numel(), float(lr), float(beta1),
                                    float(beta2), float(eps), int(step), _stream(p.device)),

@@ -562,11 +562,15 @@ int il_bin_counts(const void* x, int x_dtype, int64_t N, int64_t IN, int64_t K, 
     cudaStream_t s = (cudaStream_t)stream;
     const size_t smem = (size_t)K * sizeof(unsigned int);
     auto* cnt = reinterpret_cast<unsigned long long*>(counts);
-    if (x_dtype == IL_BF16)
-        il::bin_counts_kernel<il::kBF16><<<g, 256, smem, s>>>(x, N * IN, c, cnt);
-    else
-        il::bin_counts_kernel<il::kF32><<<g, 256, smem, s>>>(x, N * IN, c, cnt);
-    return launch_status();
+    // K > 12288 counters need more than the default 48 KB of dynamic shared memory
+    auto run = [&](auto kern) -> int {
+        if (smem > 48 * 1024 &&
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return IL_ERR_LAUNCH;
+        kern<<<g, 256, smem, s>>>(x, N * IN, c, cnt);
+        return launch_status();
+    };
+    return x_dtype == IL_BF16 ? run(il::bin_counts_kernel<il::kBF16>) : run(il::bin_counts_kernel<il::kF32>);
 }
 
 int il_adam_step(float* p, const float* g, float* m, float* v, int64_t n, double lr, double beta1,

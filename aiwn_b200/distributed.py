@@ -76,13 +76,25 @@ class TokenParallelIndexedLinear(nn.Module):
         b.grad = self._bucket[t.numel():].view_as(b)
         return self._bucket
 
+    def _grads_attached(self) -> bool:
+        """True when table.grad and bias.grad are still the bucket's views."""
+        bk = self._bucket
+        if bk is None:
+            return False
+        t, b = self.layer.table, self.layer.bias
+        return (t.grad is not None and b.grad is not None and t.grad.data_ptr() == bk.data_ptr()
+                and b.grad.data_ptr() == bk.data_ptr() + t.numel() * bk.element_size())
+
     def zero_grad(self, set_to_none: bool = False):  # noqa: D401 - keeps the bucket alive
         """Zero the gradient bucket (the .grad tensors stay views of it)."""
         self._ensure_bucket().zero_()
 
     def forward(self, x):
-        if self.layer.table.grad is None or self._bucket is None:
-            self._ensure_bucket()
+        if not self._grads_attached():
+            # First step, or an optimizer's zero_grad(set_to_none=True) (or
+            # any other code) detached .grad from the bucket: the bucket holds
+            # the previous step's sums, so it starts again from zero.
+            self._ensure_bucket().zero_()
         return self.layer(x)
 
     def sync_grads(self, async_op: bool = False):

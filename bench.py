@@ -57,6 +57,26 @@ CONFIGS = {
 }
 
 
+def arm_config(cfg):
+    """The `config` object of the JSON line: identical in both arms (the
+    workload and its sizes only; how an arm runs it goes in top-level keys)."""
+    return {"workload": cfg["desc"], "K": cfg["K"], "in_d": cfg["IN"], "out_d": cfg["OUT"],
+            "tokens_per_gpu": cfg["B"] * cfg["seq"], "d": cfg["d"], "B": cfg["B"], "seq": cfg["seq"]}
+
+
+def cpu_model() -> str:
+    """The host CPU's model name (first `model name` line of /proc/cpuinfo)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -176,8 +196,7 @@ def run_reference(args, cfg, world, rank):
         return {"metric": METRIC, "value": b["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-                "config": {"workload": cfg["desc"], "K": cfg["K"], "tokens_per_gpu": cfg["B"] * cfg["seq"]},
-                "cpu_baseline": b, "e2e": {"value": b["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "config": arm_config(cfg), "cpu_baseline": b, "e2e": {"value": b["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                                            "d2h_bytes_per_step": 0}}
     torch.set_num_threads(os.cpu_count() or 1)
     N, IN, OUT, K = cfg["B"] * cfg["seq"], cfg["IN"], cfg["OUT"], cfg["K"]
@@ -211,9 +230,9 @@ def run_reference(args, cfg, world, rank):
         "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16" if cfg["dtype"] == "bf16" else "f32", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": cfg["desc"], "K": K, "in_d": IN, "out_d": OUT, "tokens_per_gpu": N,
-                   "d": cfg["d"], "B": cfg["B"], "seq": cfg["seq"]},
-        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "config": arm_config(cfg), "x_dtype": cfg["dtype"],
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "cpu_model": cpu_model(), "kind": "port",
+                         "sample": sample},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -257,6 +276,67 @@ def reference_gpu(cfg, x, table, bias, go, reps=3):
             "reps": reps, "inputs": "the bench's first x/go set, device-resident"}
 
 
+REF_PKG = os.path.join(ROOT, "baseline", "_ref")
+
+
+def reference_triton(cfg, x, table, bias, go, reps=3):
+    """The reference's own GPU path: ``aiwn.layers.indexed_linear._Fn``
+    (Triton forward IL:23-39 + bias add, Triton dx IL:41-60, one-hot einsum
+    dtable IL:131-149, go.sum(0) dbias), installed unchanged into
+    baseline/_ref by baseline/install_ref.py and timed on the same
+    device-resident inputs as this library.  Reported beside the result, not
+    as it.  fp32 x only: its backward allocates fp32 one-hot tensors of x's
+    dtype and cannot run bf16."""
+    if cfg["dtype"] != "f32":
+        return {"unavailable": "the reference's Triton backward takes fp32 x only"}
+    if not os.path.isdir(os.path.join(REF_PKG, "aiwn")):
+        return {"unavailable": "reference package not installed (python baseline/install_ref.py)"}
+    try:
+        sys.path.insert(0, REF_PKG)
+        try:
+            import aiwn.layers.indexed_linear as ref_il
+        finally:
+            sys.path.remove(REF_PKG)
+        if not ref_il.TRITON_OK:
+            return {"unavailable": "triton did not import in the reference module"}
+        bw = 2.0 / cfg["K"]
+        xr = x.detach().clone().requires_grad_(True)
+        tr = table.detach().clone().requires_grad_(True)
+        br = bias.detach().clone().requires_grad_(True)
+
+        def fwd():
+            with torch.no_grad():
+                return ref_il._Fn.apply(xr, tr, br, bw)
+
+        def fwd_bwd():
+            out = ref_il._Fn.apply(xr, tr, br, bw)
+            return torch.autograd.grad(out, (xr, tr, br), go)
+
+        def timed(fn):
+            fn()  # warm-up (and Triton's JIT compile)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / reps
+
+        ms_f = timed(fwd)
+        ms_fb = timed(fwd_bwd)
+        n = x.shape[0]
+        return {"source": "aiwn.layers.indexed_linear._Fn (Triton), the reference package in baseline/_ref",
+                "fwd_ms": ms_f, "fwd_bwd_ms": ms_fb, "fwd_tokens_per_s": n / (ms_f * 1e-3),
+                "fwd_bwd_tokens_per_s": n / (ms_fb * 1e-3), "reps": reps,
+                "inputs": "the bench's first x/go set, device-resident"}
+    except Exception as e:  # the comparator must not take the bench line down with it
+        torch.cuda.synchronize()
+        return {"unavailable": f"{type(e).__name__}: {str(e)[:200]}"}
+    finally:
+        torch.cuda.empty_cache()
+
+
 def cpu_baseline(cfg, seconds=12.0):
     """The reference's CPU path on a bounded sample of the workload."""
     torch.set_num_threads(os.cpu_count() or 1)
@@ -273,7 +353,7 @@ def cpu_baseline(cfg, seconds=12.0):
         done += 1
     dt = (time.perf_counter() - t0) / done
     cores = torch.get_num_threads()
-    return {"value": n_s / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+    return {"value": n_s / dt, "unit": "tokens/s", "cores": cores, "cpu_model": cpu_model(), "kind": "port",
             "sample": f"{done} fwd+bwd steps of {n_s} tokens (reference eager ops{', V2 chain' if cfg.get('v2') else ''}, "
                       f"oracle/eager_port.py) in {seconds:.0f} s on {cores} threads"}
 
@@ -411,10 +491,9 @@ def run_ours_v2(args, cfg, world, rank, local):
         "metric": METRIC, "value": world * N / (ms_step * 1e-3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": cfg["desc"], "K": K, "in_d": IN, "out_d": OUT, "tokens_per_gpu": N, "d": cfg["d"],
-                   "B": cfg["B"], "seq": cfg["seq"], "x_dtype": "f32",
-                   "parallelism": f"token-parallel dp{world}" + (" + NCCL all-reduce of the gradients" if world > 1 else ""),
-                   "l2": f"inputs rotate over {n_sets} sets ({n_sets * per_set / 2**20:.0f} MiB > L2)"},
+        "config": arm_config(cfg), "x_dtype": "f32",
+        "parallelism": f"token-parallel dp{world}" + (" + NCCL all-reduce of the gradients" if world > 1 else ""),
+        "l2": f"inputs rotate over {n_sets} sets ({n_sets * per_set / 2**20:.0f} MiB > L2)",
         "fwd_tokens_per_s": world * N / (ms_fwd * 1e-3),
         "fwd_bwd_tokens_per_s": world * N / (ms_step * 1e-3),
         "ms": {"fwd": ms_fwd, "bwd": ms_bwd, "fwd_bwd": ms_step},
@@ -474,7 +553,7 @@ def gpt_cpu_baseline(cfg, seconds=12.0):
     dt = (time.perf_counter() - t0) / done
     n = Bs * GPT_CFG["block_size"]
     cores = torch.get_num_threads()
-    return {"value": n / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+    return {"value": n / dt, "unit": "tokens/s", "cores": cores, "cpu_model": cpu_model(), "kind": "port",
             "sample": f"{done} training steps of batch {Bs} x ctx {GPT_CFG['block_size']} (the reference's eager "
                       f"ops: IndexedLinear._eager restated in oracle/eager_port.py) in {seconds:.0f} s on {cores} threads"}
 
@@ -577,10 +656,9 @@ def run_ours_gpt(args, cfg, world, rank, local):
         "metric": METRIC, "value": world * n_tok / (ms_step * 1e-3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Zipf(1.1) token stream)",
-        "config": {"workload": cfg["desc"], "K": GPT_CFG["K"], "in_d": 16, "out_d": 16, "tokens_per_gpu": n_tok,
-                   "d": GPT_CFG["n_embd"], "B": B, "seq": T, "x_dtype": "f32",
-                   "parallelism": f"data-parallel dp{world}" + (" (gradient all-reduce in the graph)" if world > 1 else ""),
-                   "l2": "model and activations fit L2; steps rotate over 8 token batches"},
+        "config": arm_config(cfg), "x_dtype": "f32",
+        "parallelism": f"data-parallel dp{world}" + (" (gradient all-reduce in the graph)" if world > 1 else ""),
+        "l2": "model and activations fit L2; steps rotate over 8 token batches",
         "train_step_tokens_per_s": world * n_tok / (ms_step * 1e-3),
         "eager_step_tokens_per_s": world * n_tok / (ms_eager * 1e-3),
         "ms": {"train_step_graph": ms_step, "train_step_eager": ms_eager},
@@ -745,10 +823,9 @@ def run_ours(args, cfg, world, rank, local):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16" if sx == 2 else "f32", "data": "synthetic",
-        "config": {"workload": cfg["desc"], "K": K, "in_d": IN, "out_d": OUT, "tokens_per_gpu": N,
-                   "d": cfg["d"], "B": cfg["B"], "seq": cfg["seq"], "x_dtype": cfg["dtype"],
-                   "parallelism": f"token-parallel dp{world}" + (" + NCCL all-reduce of [dtable|dbias]" if world > 1 else ""),
-                   "l2": f"inputs rotate over {n_sets} sets of x/go/out/dx ({n_sets * per_set / 2**20:.0f} MiB > L2)"},
+        "config": arm_config(cfg), "x_dtype": cfg["dtype"],
+        "parallelism": f"token-parallel dp{world}" + (" + NCCL all-reduce of [dtable|dbias]" if world > 1 else ""),
+        "l2": f"inputs rotate over {n_sets} sets of x/go/out/dx ({n_sets * per_set / 2**20:.0f} MiB > L2)",
         "fwd_tokens_per_s": world * N / (ms_fwd * 1e-3),
         "fwd_bwd_tokens_per_s": world * N / (ms_step * 1e-3),
         "train_step_tokens_per_s": world * N / (ms_train * 1e-3),
@@ -774,6 +851,7 @@ def run_ours(args, cfg, world, rank, local):
     }
     if world == 1 and not args.no_reference_gpu:
         res["reference_gpu"] = reference_gpu(cfg, xs[0], table, bias, gos[0])
+        res["reference_triton"] = reference_triton(cfg, xs[0], table, bias, gos[0])
     if world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(cfg)
     return res

@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this directory by running the REFERENCE.
 
-Run once, in a container that has the reference checked out read-only at
-/root/reference (it is not present where the tests run)::
+Run once, where a read-only checkout of the reference is available (it is
+not present where the tests run), naming it with AIWN_REFERENCE::
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py
+    AIWN_REFERENCE=<reference checkout> PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py
 
 For every case it builds seeded CPU inputs, calls the reference module's own
 CPU path -- ``aiwn.layers.indexed_linear.IndexedLinear.forward`` on CPU
@@ -28,12 +28,20 @@ import sys
 import numpy as np
 import torch
 
-REF = "/root/reference"
+
+
+def _reference_dir() -> str:
+    ref = os.environ.get("AIWN_REFERENCE")
+    if not ref or not os.path.isdir(os.path.join(ref, "aiwn")):
+        raise SystemExit("set AIWN_REFERENCE to the reference checkout (the directory holding aiwn/)")
+    return ref
+
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 def _ref_module():
-    sys.path.insert(0, REF)
+    sys.path.insert(0, _reference_dir())
     from aiwn.layers.indexed_linear import IndexedLinear, indexed_dims  # noqa: E402
     return IndexedLinear, indexed_dims
 

@@ -1,10 +1,10 @@
 """Generate the IndexedLinearV2 golden fixtures (cdfnorm_*.npz) by running the
 REFERENCE.
 
-Run once, in a container that has the reference checked out read-only at
-/root/reference (it is not present where the tests run)::
+Run once, where a read-only checkout of the reference is available (it is
+not present where the tests run), naming it with AIWN_REFERENCE::
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden_cdfnorm.py
+    AIWN_REFERENCE=<reference checkout> PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden_cdfnorm.py
 
 Each case builds seeded CPU inputs and runs the reference's own modules on
 CPU: ``aiwn.layers.indexed_linear_v2.GaussianCDFNorm`` (LayerNorm with
@@ -23,7 +23,15 @@ import sys
 import numpy as np
 import torch
 
-REF = "/root/reference"
+
+
+def _reference_dir() -> str:
+    ref = os.environ.get("AIWN_REFERENCE")
+    if not ref or not os.path.isdir(os.path.join(ref, "aiwn")):
+        raise SystemExit("set AIWN_REFERENCE to the reference checkout (the directory holding aiwn/)")
+    return ref
+
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 CASES = [
@@ -34,7 +42,7 @@ CASES = [
 
 
 def main():
-    sys.path.insert(0, REF)
+    sys.path.insert(0, _reference_dir())
     from aiwn.layers.indexed_linear import IndexedLinear  # noqa: E402
     from aiwn.layers.indexed_linear_v2 import GaussianCDFNorm  # noqa: E402
 

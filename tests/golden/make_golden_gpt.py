@@ -1,9 +1,9 @@
 """Generate tests/golden/gpt_small.npz by running the REFERENCE's IndexedGPT.
 
-Run once, in a container that has the reference checked out read-only at
-/root/reference (it is not present where the tests run)::
+Run once, where a read-only checkout of the reference is available (it is
+not present where the tests run), naming it with AIWN_REFERENCE::
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden_gpt.py
+    AIWN_REFERENCE=<reference checkout> PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden_gpt.py
 
 Builds the reference's ``IndexedGPT`` (transformer_validation.py:295-385) at a
 small size with dropout 0 on CPU (its IndexedLinear layers take ``_eager``),
@@ -19,7 +19,15 @@ import sys
 import numpy as np
 import torch
 
-REF = "/root/reference"
+
+
+def _reference_dir() -> str:
+    ref = os.environ.get("AIWN_REFERENCE")
+    if not ref or not os.path.isdir(os.path.join(ref, "aiwn")):
+        raise SystemExit("set AIWN_REFERENCE to the reference checkout (the directory holding aiwn/)")
+    return ref
+
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 CFG = dict(vocab_size=65, block_size=32, n_layer=2, n_head=4, n_embd=64, K=16, dropout=0.0)
@@ -27,7 +35,7 @@ BATCH = 4
 
 
 def main():
-    sys.path.insert(0, REF)
+    sys.path.insert(0, _reference_dir())
     import transformer_validation as tv  # noqa: E402
     torch.manual_seed(123)
     model = tv.IndexedGPT(**CFG)

@@ -78,3 +78,17 @@ def test_get_bucket_counts_v1_and_v2():
         xn = v2.cdf(x).cpu().numpy()
     lo2, _, _ = oracle.bins(xn, K, 2.0 / K)
     assert np.array_equal(c2.cpu().numpy(), np.bincount(lo2.reshape(-1), minlength=K).astype(np.float32))
+
+
+def test_bin_counts_at_the_largest_k():
+    """K = 16384 counters take 64 KB of shared memory per CTA (above the
+    default 48 KB dynamic limit)."""
+    K = 16384
+    bw = 2.0 / K
+    g = torch.Generator().manual_seed(77)
+    x = torch.rand(4096, 24, generator=g) * 2.2 - 1.1
+    lo, _, _ = oracle.bins(x.numpy(), K, bw)
+    ref = np.bincount(lo.reshape(-1), minlength=K)
+    counts = torch.zeros(K, dtype=torch.int64, device=DEV)
+    _lib.bin_counts(x.to(DEV), K, bw, counts)
+    assert np.array_equal(counts.cpu().numpy(), ref)

@@ -115,6 +115,39 @@ def _token_parallel_worker(rank, world, port, q):
             dist.destroy_process_group()
 
 
+def _optimizer_zero_grad_worker(rank, world, port, q):
+    """torch optimizers' zero_grad() sets .grad to None by default; the next
+    forward must start the gradient bucket from zero, not from the last step."""
+    try:
+        _init(rank, world, port)
+        IN, OUT, K, N = 6, 5, 16, 64
+        layer = _CPULayer(IN, OUT, K, seed=7)
+        m = TokenParallelIndexedLinear(IN, OUT, K, layer=layer, average=False)
+        m.broadcast_parameters(0)
+        opt = torch.optim.SGD(m.parameters(), lr=0.0)  # lr 0: parameters stay put, grads are compared
+        gen = torch.Generator().manual_seed(13)
+        x = torch.rand(N, IN, generator=gen) * 2 - 1
+        go = torch.randn(N, OUT, generator=gen)
+        sh = token_shard(N, world, rank)
+        grads = []
+        for step in range(3):
+            opt.zero_grad()  # set_to_none=True
+            m(x[sh]).backward(go[sh])
+            m.sync_grads()
+            opt.step()
+            grads.append((layer.table.grad.clone(), layer.bias.grad.clone()))
+        ref = _CPULayer(IN, OUT, K, seed=7)
+        eager_forward(x, ref.table, ref.bias, ref.bw).backward(go)
+        ok = all(torch.allclose(gt, ref.table.grad, rtol=1e-5, atol=1e-6) and
+                 torch.allclose(gb, ref.bias.grad, rtol=1e-5, atol=1e-6) for gt, gb in grads)
+        q.put((rank, ok, None if ok else "gradients accumulated across optimizer.zero_grad()"))
+    except Exception as e:  # pragma: no cover
+        q.put((rank, False, repr(e)))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
 def _column_shard_worker(rank, world, port, q):
     try:
         _init(rank, world, port)
@@ -163,6 +196,10 @@ def _run(worker, world=2):
 
 def test_token_parallel_bucket_allreduce_gloo():
     _run(_token_parallel_worker, 2)
+
+
+def test_token_parallel_optimizer_zero_grad_gloo():
+    _run(_optimizer_zero_grad_worker, 2)
 
 
 def test_column_shard_forward_backward_gloo():
