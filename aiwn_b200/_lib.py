@@ -73,6 +73,10 @@ def load():
         lib.il_attention_dropout_mask.restype = ci
         lib.il_bin_counts.argtypes = [vp, ci, i64, i64, i64, f64, vp, vp]
         lib.il_bin_counts.restype = ci
+        lib.il_allreduce_scratch_bytes.argtypes = [i64, ci]
+        lib.il_allreduce_scratch_bytes.restype = i64
+        lib.il_allreduce_sum.argtypes = [vp, vp, i64, ci, ci, f64, f64, vp]
+        lib.il_allreduce_sum.restype = ci
         lib.il_kernel_launches.argtypes = []
         lib.il_kernel_launches.restype = i64
         lib.il_check_device_status.argtypes = [vp]
@@ -393,6 +397,47 @@ def adam_step(p, g, m, v, lr, beta1, beta2, eps, step: int):
         _check(load().il_adam_step(_p(p), _p(g), _p(m), _p(v), p.numel(), float(lr), float(beta1),
                                    float(beta2), float(eps), int(step), _stream(p.device)),
                "il_adam_step")
+
+
+def allreduce_scratch_bytes(n: int, world: int) -> int:
+    """Bytes of the per-rank scratch region allreduce_sum needs for n
+    elements over `world` ranks."""
+    b = int(load().il_allreduce_scratch_bytes(int(n), int(world)))
+    if b < 0:
+        raise ILError(f"allreduce_scratch_bytes: invalid n={n} or world={world}")
+    return b
+
+
+def allreduce_sum(bufs, scratch, n: int, rank: int, world: int, scale: float = 1.0, timeout_s: float = 10.0,
+                  device=None):
+    """In-place all-reduce (sum x scale) of n fp32 elements over `world`
+    GPUs: bufs / scratch are every rank's buffer and scratch region
+    addresses as mapped in this process (peer memory), 256-byte aligned."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    allreduce_caller(bufs, scratch, n, rank, world, timeout_s, dev)(scale)
+
+
+def allreduce_caller(bufs, scratch, n: int, rank: int, world: int, timeout_s: float, device):
+    """A function scale -> None that runs allreduce_sum with these fixed
+    buffers on the current stream of `device`, with the address arrays built
+    once (the per-call host cost is one C call)."""
+    if len(bufs) != world or len(scratch) != world:
+        raise ILError("allreduce_sum needs one buffer and one scratch address per rank")
+    dev = torch.device(device)
+    arr = ctypes.c_uint64 * world
+    b, f = arr(*[int(p) for p in bufs]), arr(*[int(p) for p in scratch])
+    pb, pf = ctypes.cast(b, ctypes.c_void_p), ctypes.cast(f, ctypes.c_void_p)
+    fn = load().il_allreduce_sum
+    n, rank, world, timeout_s = int(n), int(rank), int(world), float(timeout_s)
+
+    def call(scale: float = 1.0):
+        with _on_device(dev):
+            rc = fn(pb, pf, n, rank, world, float(scale), timeout_s, _stream(dev))
+        if rc:
+            _check(rc, "il_allreduce_sum")
+
+    call.keep = (b, f)  # the arrays live as long as the function
+    return call
 
 
 def kernel_launches() -> int:

@@ -21,6 +21,7 @@
 #include "il_fwd_token.cuh"
 #include "il_cdf.cuh"
 #include "il_attn.cuh"
+#include "il_allreduce.cuh"
 
 namespace {
 
@@ -586,6 +587,59 @@ int il_adam_step(float* p, const float* g, float* m, float* v, int64_t n, double
     const unsigned grid = grid_for(n, 256, sms);
     il::adam_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
         p, g, m, v, n, (float)beta1, (float)beta2, (float)eps, (float)(lr / bc1), (float)sqrt(bc2));
+    return launch_status();
+}
+
+int64_t il_allreduce_scratch_bytes(int64_t n, int world) {
+    if (n < 0 || world < 1 || world > il::kArMaxRanks) return -1;
+    return il::ar_scratch_bytes(n, world);
+}
+
+int il_allreduce_sum(float* const* bufs, void* const* scratch, int64_t n, int rank, int world, double scale,
+                     double timeout_s, void* stream) {
+    if (world < 1 || world > il::kArMaxRanks || rank < 0 || rank >= world || n < 0) return IL_ERR_SHAPE;
+    if (!(timeout_s > 0.0) || !(timeout_s <= 3600.0) || !(scale == scale)) return IL_ERR_VALUE;
+    if (!bufs || !scratch) return IL_ERR_NULL;
+    for (int p = 0; p < world; ++p) {
+        if (!bufs[p] || !scratch[p]) return IL_ERR_NULL;
+        if ((((uintptr_t)bufs[p]) | ((uintptr_t)scratch[p])) & 255) return IL_ERR_ALIGN;
+    }
+    if (n == 0) return IL_OK;
+    int sms = 0;
+    int st = check_device(&sms);
+    if (st) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    const unsigned long long tns = (unsigned long long)(timeout_s * 1e9);
+    if (n <= il::kArLLMaxElems) {
+        il::ArLLArgs a;
+        memset(&a, 0, sizeof(a));
+        a.buf = bufs[rank];
+        for (int p = 0; p < world; ++p)
+            a.stage[p] = reinterpret_cast<uint2*>(static_cast<char*>(scratch[p]) + il::ar_stage_offset());
+        a.ctr = static_cast<uint32_t*>(scratch[rank]) + il::kArCallWord;
+        a.n = n;
+        a.pairs = il::ar_ll_pairs(n, world);
+        a.rank = rank;
+        a.world = world;
+        a.scale = (float)scale;
+        a.timeout_ns = tns;
+        il::launch_allreduce_ll(a, il::ll_blocks(a.pairs, sms), s);
+        return launch_status();
+    }
+    il::ArArgs a;
+    memset(&a, 0, sizeof(a));
+    for (int p = 0; p < world; ++p) {
+        a.bufs[p] = bufs[p];
+        a.flags[p] = static_cast<uint32_t*>(scratch[p]);
+    }
+    const il::ArPlan pl = il::plan_allreduce(n, world, sms);
+    a.n = n;
+    a.chunk4 = pl.chunk4;
+    a.rank = rank;
+    a.world = world;
+    a.scale = (float)scale;
+    a.timeout_ns = tns;
+    il::launch_allreduce(a, pl, s);
     return launch_status();
 }
 

@@ -676,7 +676,97 @@ def run_ours_gpt(args, cfg, world, rank, local):
     return res
 
 
+def run_ours_column(args, cfg, world, rank, local):
+    """out_d column-sharded layout (tables too large to replicate): every rank
+    holds table[:, :, cols_r] and runs the whole global batch (B*seq tokens
+    per GPU, times the number of GPUs) on its columns.  Step: forward on the
+    local columns, NCCL all-gather of y, backward on the local columns
+    (local table gradient), NCCL all-reduce of the partial dx."""
+    from aiwn_b200 import _lib
+    from aiwn_b200.distributed import column_shard
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    N1, IN, OUT, K = cfg["B"] * cfg["seq"], cfg["IN"], cfg["OUT"], cfg["K"]
+    N = N1 * world
+    cols = column_shard(OUT, world, rank)
+    c = cols.stop - cols.start
+    if OUT % world:
+        raise SystemExit("--layout column needs out_d divisible by the GPU count")
+    bw = 2.0 / K
+    gen = torch.Generator(device=dev).manual_seed(1234)  # every rank draws the same global batch
+    x = make_x(N, IN, cfg["xdist"], cfg["dtype"], gen, dev)
+    table = (torch.randn(K, IN, OUT, generator=gen, device=dev) / math.sqrt(IN))[:, :, cols].contiguous()
+    bias = torch.zeros(c, device=dev)
+    go = torch.randn(N, c, generator=gen, device=dev)
+    y = torch.empty(N, c, device=dev)
+    y_all = torch.empty(world * N * c, device=dev)  # rank-major column blocks
+    dx = torch.empty_like(x)
+    gt = torch.empty_like(table)
+    gb = torch.empty(c, device=dev)
+
+    def fwd():
+        _lib.forward(x, table, bias, y, bw)
+        if world > 1:
+            torch.distributed.all_gather_into_tensor(y_all, y)
+
+    def bwd():
+        _lib.backward(go, x, table, dx, gt, gb, bw)
+        if world > 1:
+            torch.distributed.all_reduce(dx)
+
+    def sync_all():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    def timed(fn, reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        sync_all()
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        sync_all()
+        v = e0.elapsed_time(e1) / reps
+        if world > 1:
+            t = torch.tensor([v], device=dev, dtype=torch.float64)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            v = float(t.item())
+        return v
+
+    for _ in range(max(3, args.warmup)):
+        fwd()
+        bwd()
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    launches0 = _lib.kernel_launches()
+    ms_step = timed(lambda: (fwd(), bwd()), args.steps)
+    launches = _lib.kernel_launches() - launches0
+    ms_fwd_local = timed(lambda: _lib.forward(x, table, bias, y, bw), args.steps)
+    ms_bwd_local = timed(lambda: _lib.backward(go, x, table, dx, gt, gb, bw), args.steps)
+    clk = clocks.stop() if clocks else None
+    if rank != 0:
+        return None
+    return {
+        "metric": METRIC, "value": N / (ms_step * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if cfg["dtype"] == "bf16" else "f32",
+        "data": "synthetic", "config": arm_config(cfg), "x_dtype": cfg["dtype"],
+        "layout": f"out_d column-sharded over {world} GPUs: {c} columns and all {N} tokens per GPU",
+        "parallelism": f"column shard cs{world}" + (" + NCCL all-gather of y, all-reduce of dx" if world > 1 else ""),
+        "ms": {"fwd_bwd": ms_step, "fwd_local": ms_fwd_local, "bwd_local": ms_bwd_local,
+               "collectives": ms_step - ms_fwd_local - ms_bwd_local},
+        "fwd_bwd_tokens_per_s": N / (ms_step * 1e-3),
+        "e2e": None, "e2e_note": "the column layout is measured on device-resident inputs only",
+        "gpu_launches": launches, "clocks": clk,
+    }
+
+
 def run_ours(args, cfg, world, rank, local):
+    if args.layout == "column":
+        return run_ours_column(args, cfg, world, rank, local)
     if cfg.get("gpt"):
         return run_ours_gpt(args, cfg, world, rank, local)
     if cfg.get("v2"):
@@ -702,18 +792,32 @@ def run_ours(args, cfg, world, rank, local):
         import torch.distributed as dist
         dist.broadcast(table, 0)
     bias = torch.zeros(OUT, device=dev)
-    bucket = torch.empty(K * IN * OUT + OUT, device=dev)  # [gt | gb], all-reduced as one buffer
+    # [gt | gb], all-reduced as one buffer: in symmetric memory, summed by the
+    # library's peer-memory kernel (--exchange peer), or by NCCL
+    peer = None
+    if world > 1 and args.exchange == "peer":
+        from aiwn_b200.comm import PeerBucket
+        peer = PeerBucket(K * IN * OUT + OUT, dev)
+        bucket = peer.tensor
+    else:
+        bucket = torch.empty(K * IN * OUT + OUT, device=dev)
     gt = bucket[: K * IN * OUT].view(K, IN, OUT)
     gb = bucket[K * IN * OUT:]
     ws_n = _lib.workspace_bytes(N, IN, OUT, K, xdt)
     ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
+
+    def exchange():
+        if peer is not None:
+            peer.all_reduce(1.0)
+        else:
+            torch.distributed.all_reduce(bucket)
 
     def step(k):
         i = k % n_sets
         _lib.forward(xs[i], table, bias, outs[i], bw)
         _lib.backward(gos[i], xs[i], table, gxs[i], gt, gb, bw, ws if ws_n else None)
         if world > 1:
-            torch.distributed.all_reduce(bucket)
+            exchange()
 
     def sync_all():
         torch.cuda.synchronize(dev)
@@ -774,16 +878,30 @@ def run_ours(args, cfg, world, rank, local):
 
     # the same step without the gradient all-reduce (multi-GPU runs): the
     # difference is the exchange step's cost
-    ms_noar = None
+    ms_noar = ms_nccl = None
     if world > 1:
         def step_local(k):
             i = k % n_sets
             _lib.forward(xs[i], table, bias, outs[i], bw)
             _lib.backward(gos[i], xs[i], table, gxs[i], gt, gb, bw, ws if ws_n else None)
         ms_noar = time_calls(step_local, reps)
+        if peer is not None:
+            # the same step with NCCL's all-reduce of a plain bucket, for comparison
+            nb = torch.empty_like(bucket)
+            gtn, gbn = nb[: K * IN * OUT].view(K, IN, OUT), nb[K * IN * OUT:]
+
+            def step_nccl(k):
+                i = k % n_sets
+                _lib.forward(xs[i], table, bias, outs[i], bw)
+                _lib.backward(gos[i], xs[i], table, gxs[i], gtn, gbn, bw, ws if ws_n else None)
+                torch.distributed.all_reduce(nb)
+            for k in range(3):
+                step_nccl(k)
+            ms_nccl = time_calls(step_nccl, reps)
 
     # end to end through the public module API, host buffers, copies inside
-    m = TokenParallelIndexedLinear(IN, OUT, K, layer=IndexedLinear(IN, OUT, K)).to(dev)
+    m = TokenParallelIndexedLinear(IN, OUT, K, layer=IndexedLinear(IN, OUT, K),
+                                   exchange="peer" if args.exchange == "peer" else "nccl").to(dev)
     with torch.no_grad():
         m.table.copy_(table)
     xh = [x.cpu().pin_memory() for x in xs[:2]]
@@ -824,7 +942,9 @@ def run_ours(args, cfg, world, rank, local):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16" if sx == 2 else "f32", "data": "synthetic",
         "config": arm_config(cfg), "x_dtype": cfg["dtype"],
-        "parallelism": f"token-parallel dp{world}" + (" + NCCL all-reduce of [dtable|dbias]" if world > 1 else ""),
+        "parallelism": f"token-parallel dp{world}" + (
+            (" + peer-memory all-reduce of [dtable|dbias] (il_allreduce_sum, NVLink)" if peer is not None
+             else " + NCCL all-reduce of [dtable|dbias]") if world > 1 else ""),
         "l2": f"inputs rotate over {n_sets} sets of x/go/out/dx ({n_sets * per_set / 2**20:.0f} MiB > L2)",
         "fwd_tokens_per_s": world * N / (ms_fwd * 1e-3),
         "fwd_bwd_tokens_per_s": world * N / (ms_step * 1e-3),
@@ -832,6 +952,8 @@ def run_ours(args, cfg, world, rank, local):
         "ms": {"fwd": ms_fwd, "bwd": ms_bwd, "fwd_bwd": ms_step, "train_step_adam": ms_train},
         **({"fwd_bwd_without_allreduce": {"tokens_per_s": world * N / (ms_noar * 1e-3), "ms": ms_noar}}
            if ms_noar is not None else {}),
+        **({"fwd_bwd_nccl_allreduce": {"tokens_per_s": world * N / (ms_nccl * 1e-3), "ms": ms_nccl}}
+           if ms_nccl is not None else {}),
         "hbm_roofline_frac": {
             "fwd": b_fwd / (ms_fwd * 1e-3) / 1e9 / hbm,
             "fwd_bwd": (b_fwd + b_bwd) / (ms_step * 1e-3) / 1e9 / hbm,
@@ -864,6 +986,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c3")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="gradient all-reduce at N>1: the library's peer-memory kernel or NCCL")
+    ap.add_argument("--layout", choices=["token", "column"], default="token",
+                    help="token: replicated table, tokens sharded (default); column: out_d column-sharded")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip timing the reference's own CUDA extension (when built)")

@@ -205,6 +205,30 @@ IL_API int il_cdf_backward(const float* gxn, const float* x, const float* gamma,
                     int64_t IN, void* stream);
 
 /*
+ * In-place all-reduce (sum, times `scale`) of an fp32 buffer of n elements
+ * across the `world` GPUs of one NVLink/NVSwitch node, one process (rank) per
+ * GPU.  bufs[p] and scratch[p] (HOST arrays of `world` device addresses) are
+ * rank p's buffer and scratch region as mapped in this process (peer-
+ * accessible memory, e.g. torch symmetric memory); bufs[rank] and
+ * scratch[rank] are this rank's own.  Every address is 256-byte aligned;
+ * each scratch region holds il_allreduce_scratch_bytes(n, world) bytes,
+ * zeroed on every rank (and all ranks past a host barrier) before the first
+ * call.  Every rank makes the same sequence of calls with the same n.  One
+ * kernel, enqueued on `stream`: up to 2^21 elements, every value travels
+ * with its call's flag in one 64-bit word (pushed to the reducing rank, then
+ * the sums pushed back), so no fence or barrier is needed; larger buffers
+ * take a two-shot kernel (peer loads reduce, peer stores deliver) with
+ * per-block flag barriers.  Waits are bounded by timeout_s; on expiry
+ * il_check_device_status reports IL_ERR_TIMEOUT.  world <= 16.  The
+ * reference has no multi-GPU path; this is the gradient exchange of
+ * token-parallel training, summing the table and bias gradients of
+ * aiwn/layers/indexed_linear.py:131-151 over the ranks' tokens.
+ */
+IL_API int64_t il_allreduce_scratch_bytes(int64_t n, int world);
+IL_API int il_allreduce_sum(float* const* bufs, void* const* scratch, int64_t n, int rank, int world,
+                            double scale, double timeout_s, void* stream);
+
+/*
  * Number of kernels this library has launched in the process so far
  * (host-side counter, all devices and threads).  Lets a caller count the
  * library's launches inside a timed region.

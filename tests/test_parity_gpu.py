@@ -71,6 +71,18 @@ def test_parity_vs_oracle(c, paths, monkeypatch):
     check_against_oracle(c, x, table, bias, go)
 
 
+def test_c4_parity_at_the_bench_launch_size():
+    """The large-table configuration at the size one GPU runs in the bench:
+    16384 tokens, in_d = out_d = 1024, K = 64, x = clamp(N(0, 0.5), -1, 1).
+    Exercises the streamed forward's multi-tile path and the sorted backward's
+    128-column j-ranges with atomically added dx at that launch shape; every
+    output and gradient is compared with the oracle."""
+    from il_cases import Case
+    c = Case("c4_bench_launch", 16384, 1024, 1024, 64, "clamp_normal", "f32", 0.1, 40)
+    x, table, bias, go = make_inputs(c)
+    check_against_oracle(c, x, table, bias, go)
+
+
 @pytest.mark.parametrize("name", case_names())
 def test_parity_vs_golden(name):
     d = load_case(name)
