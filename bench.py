@@ -901,7 +901,7 @@ def run_ours(args, cfg, world, rank, local):
 
     # end to end through the public module API, host buffers, copies inside
     m = TokenParallelIndexedLinear(IN, OUT, K, layer=IndexedLinear(IN, OUT, K),
-                                   exchange="peer" if args.exchange == "peer" else "nccl").to(dev)
+                                   exchange="peer" if (world > 1 and args.exchange == "peer") else "nccl").to(dev)
     with torch.no_grad():
         m.table.copy_(table)
     xh = [x.cpu().pin_memory() for x in xs[:2]]
