@@ -22,6 +22,7 @@
 #include "il_cdf.cuh"
 #include "il_attn.cuh"
 #include "il_allreduce.cuh"
+#include "il_tc.cuh"
 
 namespace {
 
@@ -109,6 +110,18 @@ inline unsigned grid_for(int64_t work, int threads, int num_sms) {
 // kernel selection of the forward (arguments already checked)
 int forward_dispatch(const void* x, int x_dtype, const float* table, const float* bias, float* out, int64_t N,
                      int64_t IN, int64_t OUT, const il::BinCfg& c, int sms, cudaStream_t s) {
+    // AIWN_IL_FORWARD=tc: the tensor-core (hat-basis GEMM) forward where it applies
+    const char* fv = getenv("AIWN_IL_FORWARD");
+    if (fv && strcmp(fv, "tc") == 0 && il::tc_forward_ok(N, IN, OUT, c.K, c)) {
+        const int rc = il::tc_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, s);
+        if (rc != il::kNotApplicable) {
+            if (rc) {
+                cudaGetLastError();
+                return IL_ERR_LAUNCH;
+            }
+            return launch_status();
+        }
+    }
     const KernelChoice path = kernel_choice("AIWN_IL_FORWARD", "token", "cluster");
     // Rows of a multiple of 32 outputs over few bins (K <= 64): the cluster
     // kernel's lanes read consecutive chunks of one table row, and it beat the

@@ -54,6 +54,11 @@ CONFIGS = {
     "c5": dict(desc="IndexedGPT projection shape IndexedLinear(16, 16, K=128), batch 64 x ctx 256 "
                     "(16384 tokens), x~U(-1,1) fp32", d=256, K=128, B=64, seq=256, IN=16, OUT=16,
                xdist="uniform", dtype="f32"),
+    "c5qkv": dict(desc="IndexedGPT fused q|k|v projection IndexedLinear(16, 48, K=128), batch 64 x ctx 256 "
+                       "(16384 tokens), x~U(-1,1) fp32", d=256, K=128, B=64, seq=256, IN=16, OUT=48,
+                  xdist="uniform", dtype="f32"),
+    "c1big": dict(desc="IndexedLinear(64, 64, K=16) at 131072 tokens (the C1 layer, large batch), x~U(-1,1) fp32",
+                  d=256, K=16, B=32, seq=4096, IN=64, OUT=64, xdist="uniform", dtype="f32"),
 }
 
 

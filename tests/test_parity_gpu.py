@@ -5,6 +5,8 @@ Tolerances (normwise, see golden_io.normwise_close): forward 1e-5 relative in
 fp32 and 2e-2 with bf16 x; fp32 gradients 1e-4; bf16 gx 2e-2.  Bins are
 bit-exact.
 """
+import math
+
 import numpy as np
 import pytest
 import torch
@@ -69,6 +71,41 @@ def test_parity_vs_oracle(c, paths, monkeypatch):
     monkeypatch.setenv("AIWN_IL_BACKWARD", paths[1])
     x, table, bias, go = make_inputs(c)
     check_against_oracle(c, x, table, bias, go)
+
+
+TC_CASES = [c for c in CASES + EDGE_CASES
+            if c.OUT % 16 == 0 and c.OUT <= 256 and c.K >= 16 and (c.K & (c.K - 1)) == 0 and (c.IN * c.K) % 32 == 0]
+
+
+@pytest.mark.parametrize("c", TC_CASES, ids=lambda c: c.name)
+def test_tensor_core_forward_vs_oracle(c, monkeypatch):
+    """The tcgen05 hat-basis forward (3xTF32, accumulator in tensor memory),
+    pinned with AIWN_IL_FORWARD=tc, on every listed shape it takes."""
+    monkeypatch.setenv("AIWN_IL_FORWARD", "tc")
+    x, table, bias, _ = make_inputs(c)
+    out = torch.empty(c.N, c.OUT, device=DEV)
+    _lib.forward(x.to(DEV), table.to(DEV), bias.to(DEV), out, 2.0 / c.K)
+    ref = oracle.forward(x_numpy(x), table.numpy(), bias.numpy(), 2.0 / c.K, x_dtype=c.dtype)
+    normwise_close(out.cpu().numpy(), ref, FWD_RTOL[c.dtype], f"{c.name} out (tc)")
+
+
+def test_tensor_core_forward_nonfinite_and_partial_tile(monkeypatch):
+    """Tokens with +-inf or NaN inputs take the plain formula in the
+    epilogue; 300 tokens end in a partial 128-token tile."""
+    monkeypatch.setenv("AIWN_IL_FORWARD", "tc")
+    g = torch.Generator().manual_seed(5)
+    N, IN, OUT, K = 300, 8, 32, 16
+    x = torch.rand(N, IN, generator=g) * 2.4 - 1.2
+    x[3, 1] = float("inf")
+    x[4, 0] = float("-inf")
+    x[7, 5] = float("nan")
+    x[299, 2] = float("inf")
+    table = torch.randn(K, IN, OUT, generator=g) / math.sqrt(IN)
+    bias = torch.randn(OUT, generator=g) * 0.1
+    out = torch.empty(N, OUT, device=DEV)
+    _lib.forward(x.to(DEV), table.to(DEV), bias.to(DEV), out, 2.0 / K)
+    ref = oracle.forward(x.numpy(), table.numpy(), bias.numpy(), 2.0 / K)
+    normwise_close(out.cpu().numpy(), ref, FWD_RTOL["f32"], "tc non-finite")
 
 
 def test_c4_parity_at_the_bench_launch_size():
