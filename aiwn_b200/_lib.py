@@ -46,6 +46,8 @@ def load():
         lib.il_version.restype = ctypes.c_char_p
         lib.il_forward.argtypes = [vp, ci, vp, vp, vp, i64, i64, i64, i64, f64, vp]
         lib.il_forward.restype = ci
+        lib.il_forward_counts.argtypes = [vp, ci, vp, vp, vp, i64, i64, i64, i64, f64, vp, vp]
+        lib.il_forward_counts.restype = ci
         lib.il_workspace_bytes.argtypes = [i64, i64, i64, i64, ci]
         lib.il_workspace_bytes.restype = i64
         lib.il_backward.argtypes = [vp, vp, ci, vp, vp, vp, vp, i64, i64, i64, i64, f64, vp, i64, vp]
@@ -178,18 +180,26 @@ def x_dtype_code(x: torch.Tensor) -> int:
         raise ILError(f"x dtype {x.dtype} is not supported (float32 or bfloat16)") from None
 
 
-def forward(x, table, bias, out, bw: float):
-    """out[N, OUT] (fp32) <- IndexedLinear forward of x[N, IN]."""
-    _same_device(x, table, bias, out)
+def forward(x, table, bias, out, bw: float, counts=None):
+    """out[N, OUT] (fp32) <- IndexedLinear forward of x[N, IN]; with
+    ``counts`` (int64 [K] on the device) the bin occupancy of x is added into
+    it by the same launch where the kernel allows."""
+    _same_device(x, table, bias, out, counts)
     N, IN, OUT, K = _layer_shapes(x, table)
     x_dtype_code(x)
     _expect("bias", bias, (OUT,))
     _expect("out", out, (N, OUT))
-    _need_cuda(x, table, bias, out)
+    _expect("counts", counts, (K,), torch.int64)
+    _need_cuda(x, table, bias, out, counts)
     lib = load()
     with _on_device(x.device):
-        _check(lib.il_forward(_p(x), x_dtype_code(x), _p(table), _p(bias), _p(out),
-                              N, IN, OUT, K, float(bw), _stream(x.device)), "il_forward")
+        if counts is None:
+            _check(lib.il_forward(_p(x), x_dtype_code(x), _p(table), _p(bias), _p(out),
+                                  N, IN, OUT, K, float(bw), _stream(x.device)), "il_forward")
+        else:
+            _check(lib.il_forward_counts(_p(x), x_dtype_code(x), _p(table), _p(bias), _p(out),
+                                         N, IN, OUT, K, float(bw), _p(counts), _stream(x.device)),
+                   "il_forward_counts")
     return out
 
 

@@ -3,10 +3,13 @@
 ``get_bucket_counts`` (aiwn/experiments/bucket_analysis.py:33-51).
 
 The reference copies every tracked activation to the host and runs
-``torch.bincount`` there.  Here the counts come from ``il_bin_counts``: the
-library's bit-exact bins, counted in shared memory on the device and added
-into a 64-bit device accumulator, so a tracked forward costs one small kernel
-and no copy.  ``counts`` / ``entropy()`` read the accumulator back when asked.
+``torch.bincount`` there.  Here the counts are the library's bit-exact bins,
+counted in shared memory on the device and added into a 64-bit device
+accumulator.  For this package's IndexedLinear the forward kernel itself
+counts while it bins (``il_forward_counts``: the layer's eval-mode forwards
+add into the tracker's accumulator); other modules get a forward pre-hook
+that runs ``il_bin_counts`` on their input.  ``counts`` / ``entropy()`` read
+the accumulator back when asked.
 """
 from __future__ import annotations
 
@@ -25,6 +28,7 @@ class BucketTracker:
         self.K = K
         self._acc = {}  # device -> int64 [K]
         self.handles = []
+        self._fused = []  # IndexedLinear layers that count in their forward kernel
 
     def _dev_counts(self, dev):
         acc = self._acc.get(dev)
@@ -46,6 +50,13 @@ class BucketTracker:
             acc.zero_()
 
     def register(self, layer):
+        from .layers.indexed_linear import IndexedLinear
+        if isinstance(layer, IndexedLinear) and layer.K == self.K and layer.table.is_cuda:
+            # the layer's forward kernel adds into the accumulator itself
+            layer._bin_counts = self._dev_counts(layer.table.device)
+            self._fused.append(layer)
+            return
+
         def hook(module, args):
             if not module.training:
                 xf = args[0].reshape(-1, module.in_dim).detach()
@@ -64,6 +75,9 @@ class BucketTracker:
         for h in self.handles:
             h.remove()
         self.handles.clear()
+        for layer in self._fused:
+            layer._bin_counts = None
+        self._fused.clear()
 
 
 def get_bucket_counts(layer, x: torch.Tensor, K: int) -> torch.Tensor:

@@ -257,6 +257,35 @@ int il_forward(const void* x, int x_dtype, const float* table, const float* bias
     return forward_dispatch(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s);
 }
 
+int il_forward_counts(const void* x, int x_dtype, const float* table, const float* bias, float* out, int64_t N,
+                      int64_t IN, int64_t OUT, int64_t K, double bw, uint64_t* counts, void* stream) {
+    int st = check_common(x, x_dtype, N, IN, K, bw);
+    if (st) return st;
+    if (OUT < 1 || K > 16384) return IL_ERR_SHAPE;
+    if (N == 0) return IL_OK;
+    if (!table || !bias || !out || !counts) return IL_ERR_NULL;
+    if ((uintptr_t)counts & 7) return IL_ERR_ALIGN;
+    int sms = 0;
+    if ((st = check_device(&sms))) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    const il::BinCfg c = make_cfg(bw, K);
+    auto* cnt = reinterpret_cast<unsigned long long*>(counts);
+    // the token forward counts while it bins; other shapes take the forward and a counting pass
+    if (kernel_choice("AIWN_IL_FORWARD", "token", "cluster") != kOnlyOther &&
+        il::fast_forward_args_ok(x, x_dtype, table, bias, out, N, IN, OUT, c.K, c)) {
+        const int rc = il::token_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s, cnt);
+        if (rc != il::kNotApplicable) {
+            if (rc) {
+                cudaGetLastError();
+                return IL_ERR_LAUNCH;
+            }
+            return launch_status();
+        }
+    }
+    if ((st = forward_dispatch(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s))) return st;
+    return il_bin_counts(x, x_dtype, N, IN, K, bw, counts, stream);
+}
+
 int il_cdf_forward(const float* x, const float* gamma, const float* beta, double eps, const float* table,
                    const float* bias, float* xn, float* mean, float* rstd, float* out, int64_t N, int64_t IN,
                    int64_t OUT, int64_t K, double bw, void* stream) {

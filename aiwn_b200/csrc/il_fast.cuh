@@ -128,6 +128,7 @@ struct FwdArgs {
     int slice_bytes;  // shared-memory stride between slices
     int ntiles;       // token tiles
     BinCfg cfg;
+    unsigned long long* counts = nullptr;  // token kernel: bin-occupancy histogram [K] added into (or none)
 };
 
 #ifndef IL_FWD_THREADS

@@ -36,7 +36,14 @@ __host__ __device__ constexpr int tok_threads(int C) { return C <= 2 ? 1024 : 51
 // Each CTA owns the contiguous token range [blockIdx.x * p.ntiles, ...) of
 // p.ntiles tokens (here `ntiles` is the range length) and walks it in steps of
 // one token per thread, so that the work per SM is balanced to the token.
-template <int DT, int C>
+//
+// With CNT the kernel also adds the bin-occupancy histogram of x into
+// p.counts (the bincount of aiwn/experiments/bucket_analysis.py:44-47 and
+// transformer_validation.py:105-108): CTA (range, j-range y) counts input
+// columns i with i % gridDim.y == y, so every (token, column) is counted once
+// and the counting is spread over all CTAs, into K shared-memory counters
+// flushed with one 64-bit atomic per non-empty bin.
+template <int DT, int C, bool CNT>
 __global__ void __launch_bounds__(tok_threads(C), 1)
     fwd_token_kernel(const __grid_constant__ CUtensorMap tmap, const FwdArgs p) {
     constexpr int kTokThreads = tok_threads(C);
@@ -61,6 +68,10 @@ __global__ void __launch_bounds__(tok_threads(C), 1)
                 tma_load_3d(table_s + s * p.slice_bytes + b * box_bytes, &tmap, bar, j0, s, b * p.KB);
     };
 
+    // bin counters (CNT) after the mbarriers
+    unsigned int* scnt = reinterpret_cast<unsigned int*>(smem + (bar0 + 8u * (uint32_t)nbar - smem_addr(smem)));
+    if constexpr (CNT)
+        for (int k = threadIdx.x; k < p.K; k += kTokThreads) scnt[k] = 0u;
     if (threadIdx.x == 0) {
         prefetch_tensormap(&tmap);
         for (int g = 0; g < nbar; ++g) mbar_init(bar0 + 8u * (uint32_t)g, 1);
@@ -132,6 +143,8 @@ __global__ void __launch_bounds__(tok_threads(C), 1)
                 int lo;
                 float wa, wc;
                 gather_weights<DT>(xv[q], p.cfg, lo, wa, wc);
+                if constexpr (CNT)
+                    if (n < r1 && (sb + q) % (int)gridDim.y == (int)blockIdx.y) atomicAdd(scnt + lo, 1u);
                 const uint32_t row = table_s + (uint32_t)((sb + q) * p.slice_bytes) + (uint32_t)lo * row_bytes;
 #pragma unroll
                 for (int c = 0; c < C; ++c) {
@@ -158,6 +171,11 @@ __global__ void __launch_bounds__(tok_threads(C), 1)
             }
         }
     }
+    if constexpr (CNT) {
+        __syncthreads();
+        for (int k = threadIdx.x; k < p.K; k += kTokThreads)
+            if (scnt[k]) atomicAdd(p.counts + k, (unsigned long long)scnt[k]);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -168,7 +186,7 @@ constexpr int kTokChunks[] = {8, 5, 4, 2, 1};
 // j-range width: the widest whose slices of every input column fit one CTA's
 // shared memory, narrowed while the token ranges alone would leave SMs idle
 // (a narrower j-range gives more CTAs per token range)
-inline bool plan_token_forward(int64_t N, int K, int IN, int OUT, int sms, FwdPlan& pl) {
+inline bool plan_token_forward(int64_t N, int K, int IN, int OUT, int sms, FwdPlan& pl, bool counts = false) {
     if (OUT % 4 != 0) return false;
     const int chunks = OUT / 4;
     bool found = false;
@@ -181,7 +199,8 @@ inline bool plan_token_forward(int64_t N, int K, int IN, int OUT, int sms, FwdPl
         const int KB = round_up(ceil_div(K, nb), m);
         if (KB > 256) continue;
         const int slice = round_up(std::max(KB * nb, K + 1) * RS * 4, 128);
-        const int64_t smem = (int64_t)IN * slice + 128 + 8 * ceil_div(IN, kTokXB);  // + alignment + mbarriers
+        const int64_t smem = (int64_t)IN * slice + 128 + 8 * ceil_div(IN, kTokXB) +  // + alignment + mbarriers
+                             (counts ? 4 * (int64_t)K : 0);                          // + bin counters
         if (smem > kSmemBudget) continue;
         pl = {C, 1, JR, IN, KB, nb, slice, (int)smem};
         pl.RS = RS;
@@ -195,7 +214,7 @@ inline bool plan_token_forward(int64_t N, int K, int IN, int OUT, int sms, FwdPl
 template <int DT, int C>
 inline int launch_token_fwd(const CUtensorMap& map, const FwdArgs& a, const FwdPlan& pl, int sms,
                             cudaStream_t s) {
-    auto kern = fwd_token_kernel<DT, C>;
+    auto kern = a.counts ? fwd_token_kernel<DT, C, true> : fwd_token_kernel<DT, C, false>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem) != cudaSuccess)
         return 4;
     const int jranges = ceil_div(a.OUT, pl.JR);
@@ -226,12 +245,14 @@ inline int launch_token_fwd_c(const CUtensorMap& map, const FwdArgs& a, const Fw
 
 // kNotApplicable when the table slices of all input columns do not fit one CTA
 inline int token_forward(const void* x, int x_dtype, const float* table, const float* bias, float* out,
-                         int64_t N, int64_t IN, int64_t OUT, const BinCfg& c, int sms, cudaStream_t s) {
+                         int64_t N, int64_t IN, int64_t OUT, const BinCfg& c, int sms, cudaStream_t s,
+                         unsigned long long* counts = nullptr) {
     FwdPlan pl;
-    if (!plan_token_forward(N, c.K, (int)IN, (int)OUT, sms, pl)) return kNotApplicable;
+    if (!plan_token_forward(N, c.K, (int)IN, (int)OUT, sms, pl, counts != nullptr)) return kNotApplicable;
     CUtensorMap map;
     if (!make_table_map(&map, table, c.K, (int)IN, (int)OUT, pl.RS, pl.KB)) return kNotApplicable;
     FwdArgs a;
+    a.counts = counts;
     a.x = x;
     a.bias = bias;
     a.out = out;

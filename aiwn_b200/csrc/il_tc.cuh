@@ -132,7 +132,7 @@ __device__ __forceinline__ void tc_issue_raw(const CUtensorMap* map, const TcArg
     const int st = c % kTcRaw;
     const uint32_t dst = raw0 + (uint32_t)st * raw_bytes, bar = rawbar0 + 8u * (uint32_t)st;
     const int q0 = c * kTcKC;
-    fence_proxy_async_smem();
+    // (the builders' reads of this stage are ordered before by the mbarrier they arrived on)
     mbar_arrive_expect_tx(bar, raw_bytes);
     if (p.K >= kTcKC) {
         tma_load_3d(dst, map, bar, 0, q0 / p.K, q0 % p.K);
@@ -208,19 +208,22 @@ __global__ void __launch_bounds__(kTcThreads + 32, 1)
             prefetch_tensormap(&tmap);
             for (int c = 0; c < kTcRaw; ++c) tc_issue_raw(&tmap, p, c, raw0, raw_bar0, raw_bytes);
             const uint32_t idesc = tc_idesc_tf32(kTcM, OUT);
+            // descriptors of stage 0's operands; a stage or K step moves only the
+            // start-address field (16-byte units, low bits of the descriptor)
+            const uint64_t ah0 = tc_desc(base, kTcM * 16, 128), al0 = tc_desc(base + a_bytes, kTcM * 16, 128);
+            const uint64_t bh0 = tc_desc(base + 2 * a_bytes, (uint32_t)OUT * 16, 128);
+            const uint64_t bl0 = tc_desc(base + 2 * a_bytes + b_bytes, (uint32_t)OUT * 16, 128);
+            const uint64_t astep = (2u * kTcM * 16) >> 4, bstep = (2u * (uint32_t)OUT * 16) >> 4;
             for (int c = 0; c < p.nchunk; ++c) {
                 const int st = c % S;
-                const uint32_t sa = base + (uint32_t)st * (uint32_t)p.stage_bytes;
+                const uint64_t so = ((uint64_t)st * (uint64_t)p.stage_bytes) >> 4;
                 ok &= mbar_wait_bounded(full0 + 8u * st, (uint32_t)((c / S) & 1));  // stage built
                 tc_fence_after();
 #pragma unroll
                 for (int s = 0; s < kTcKC / 8; ++s) {
                     // K = 8 per MMA: two 16-byte K groups
-                    const uint32_t ao = (uint32_t)(2 * s) * (kTcM * 16), bo = (uint32_t)(2 * s) * ((uint32_t)OUT * 16);
-                    const uint64_t ah = tc_desc(sa + ao, kTcM * 16, 128);
-                    const uint64_t al = tc_desc(sa + a_bytes + ao, kTcM * 16, 128);
-                    const uint64_t bh = tc_desc(sa + 2 * a_bytes + bo, (uint32_t)OUT * 16, 128);
-                    const uint64_t bl = tc_desc(sa + 2 * a_bytes + b_bytes + bo, (uint32_t)OUT * 16, 128);
+                    const uint64_t ah = ah0 + so + s * astep, al = al0 + so + s * astep;
+                    const uint64_t bh = bh0 + so + s * bstep, bl = bl0 + so + s * bstep;
                     tc_mma_tf32(tmem, ah, bh, idesc, (c > 0 || s > 0) ? 1u : 0u);
                     tc_mma_tf32(tmem, al, bh, idesc, 1u);
                     tc_mma_tf32(tmem, ah, bl, idesc, 1u);

@@ -66,6 +66,28 @@ class _Fn(torch.autograd.Function):
         return gx, gt, gb, None
 
 
+class _FnCounts(_Fn):
+    """_Fn whose forward also adds the bin occupancy of x into ``counts``
+    (int64 [K] on the device) -- the BucketTracker path.  Same backward."""
+
+    @staticmethod
+    def forward(ctx, x, tab, bias, bw, counts):
+        if x.dim() != 2 or tab.dim() != 3 or tab.shape[1] != x.shape[1]:
+            raise ValueError(f"_Fn: x {tuple(x.shape)} and table {tuple(tab.shape)} do not match")
+        x = x.contiguous()
+        tab = tab.contiguous()
+        bias = bias.contiguous()
+        out = torch.empty(x.shape[0], tab.shape[2], dtype=torch.float32, device=x.device)
+        _lib.forward(x, tab, bias, out, bw, counts=counts)
+        ctx.save_for_backward(x, tab)
+        ctx.bw = bw
+        return out
+
+    @staticmethod
+    def backward(ctx, go):
+        return (*_Fn.backward(ctx, go), None)
+
+
 def grad_pair(shape_a, shape_b, device, need_a: bool, need_b: bool):
     """Two fp32 gradient outputs (None where not needed).  When both are
     needed they share one allocation with b right after a, so the library
@@ -92,6 +114,9 @@ class IndexedLinear(nn.Module):
         std = math.sqrt(math.sqrt(3.0 / in_d) * (2.0 / K))
         self.table = nn.Parameter(torch.randn(K, in_d, out_d) * std)
         self.bias = nn.Parameter(torch.zeros(out_d))
+        # int64 [K] device accumulator that eval-mode forwards add their bin
+        # occupancy into (set by BucketTracker.register; None: no counting)
+        self._bin_counts = None
 
     def _eager(self, x: torch.Tensor) -> torch.Tensor:
         """The reference's name for the flattened call (IL:173).  Here it runs
@@ -103,6 +128,11 @@ class IndexedLinear(nn.Module):
             raise RuntimeError("aiwn_b200.IndexedLinear runs on CUDA (B200) only; got a CPU tensor")
         if not TRITON_OK:
             raise RuntimeError(f"libaiwn_il.so is not built ({_lib.library_path()})")
+        counts = self._bin_counts
+        if counts is not None and not self.training:
+            if counts.device != xf.device:
+                raise RuntimeError("the bin-count accumulator is on another device than the input")
+            return _FnCounts.apply(xf, self.table, self.bias, self.bw, counts)
         return _Fn.apply(xf, self.table, self.bias, self.bw)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:

@@ -87,6 +87,18 @@ IL_API int il_forward(const void* x, int x_dtype, const float* table, const floa
                int64_t N, int64_t IN, int64_t OUT, int64_t K, double bw, void* stream);
 
 /*
+ * il_forward that also adds the bin-occupancy histogram of x into counts[K]
+ * (uint64, K <= 16384; the bins of il_bins): the forward kernel that keeps
+ * every input column's table slice resident counts while it bins, other
+ * shapes run the forward and then il_bin_counts.  Replaces the forward of a
+ * layer tracked by the reference's BucketTracker (transformer_validation.py:
+ * 92-123: a forward hook copying the input to the host for torch.bincount).
+ */
+IL_API int il_forward_counts(const void* x, int x_dtype, const float* table, const float* bias, float* out,
+                             int64_t N, int64_t IN, int64_t OUT, int64_t K, double bw, uint64_t* counts,
+                             void* stream);
+
+/*
  * Bytes of device workspace il_backward needs for these sizes (0 if none).
  */
 IL_API int64_t il_workspace_bytes(int64_t N, int64_t IN, int64_t OUT, int64_t K, int x_dtype);

@@ -92,3 +92,40 @@ def test_bin_counts_at_the_largest_k():
     counts = torch.zeros(K, dtype=torch.int64, device=DEV)
     _lib.bin_counts(x.to(DEV), K, bw, counts)
     assert np.array_equal(counts.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("shape", [(131072, 20, 20, 512, "uniform", "f32"), (131072, 20, 20, 128, "tanh", "bf16"),
+                                   (16384, 16, 16, 128, "uniform", "f32"), (3000, 16, 48, 128, "wide", "f32"),
+                                   (600, 300, 8, 256, "wide", "f32")],
+                         ids=["c3", "c2_bf16", "c5", "qkv_wide", "streamed_table"])
+def test_forward_counts_equal_bincount_and_plain_forward(shape):
+    """il_forward_counts: the histogram of the forward's own bins (fused into
+    the token kernel; the streamed-table shape takes forward + counting pass)
+    equals the oracle's bincount, and the output equals il_forward's bit for
+    bit."""
+    N, IN, OUT, K, xdist, dt = shape
+    g = torch.Generator().manual_seed(N + IN + K)
+    if xdist == "uniform":
+        x = torch.rand(N, IN, generator=g) * 2 - 1
+    elif xdist == "tanh":
+        x = torch.tanh(torch.randn(N, IN, generator=g))
+    else:
+        x = torch.rand(N, IN, generator=g) * 3 - 1.5
+    if dt == "bf16":
+        x = x.to(torch.bfloat16)
+    table = torch.randn(K, IN, OUT, generator=g) / math.sqrt(IN)
+    bias = torch.randn(OUT, generator=g) * 0.1
+    xd, td, bd = x.to(DEV), table.to(DEV), bias.to(DEV)
+    bw = 2.0 / K
+    counts = torch.zeros(K, dtype=torch.int64, device=DEV)
+    o1 = torch.empty(N, OUT, device=DEV)
+    o2 = torch.empty(N, OUT, device=DEV)
+    _lib.forward(xd, td, bd, o1, bw, counts=counts)
+    _lib.forward(xd, td, bd, o2, bw)
+    assert torch.equal(o1, o2)
+    xn = x.contiguous().view(torch.int16).numpy().view(np.uint16) if dt == "bf16" else x.numpy()
+    lo, _, _ = oracle.bins(xn, K, bw, x_dtype=dt)
+    ref = np.bincount(lo.reshape(-1), minlength=K)
+    assert np.array_equal(counts.cpu().numpy(), ref)
+    _lib.forward(xd, td, bd, o1, bw, counts=counts)  # accumulates
+    assert np.array_equal(counts.cpu().numpy(), 2 * ref)
