@@ -109,6 +109,12 @@ def get_d_idx(n_embd: int, K: int, n_head: int) -> tuple:
     return d_idx, ff_idx
 
 
+def _observed(m) -> bool:
+    """Whether a layer's own forward must run: forward hooks, or a
+    BucketTracker accumulator that the layer's forward kernel adds into."""
+    return bool(m._forward_pre_hooks or m._forward_hooks or getattr(m, "_bin_counts", None) is not None)
+
+
 class IndexedAttention(nn.Module):
     """Causal multi-head attention with IndexedLinear q/k/v/c projections.
 
@@ -145,7 +151,7 @@ class IndexedAttention(nn.Module):
         backward instead of three of each."""
         projs = (self.q_proj, self.k_proj, self.v_proj)
         if (self.fused and h.is_cuda and h.dtype == torch.float32 and TRITON_OK
-                and not any(m._forward_pre_hooks or m._forward_hooks for m in projs)):
+                and not any(_observed(m) for m in projs)):
             tab = torch.cat([m.table for m in projs], dim=2)
             bias = torch.cat([m.bias for m in projs])
             qkv = _Fn.apply(h.contiguous(), tab, bias, self.q_proj.bw).view(B, T, 3 * self.d_idx)
@@ -202,8 +208,8 @@ class IndexedFFN(nn.Module):
         xf = x.reshape(-1, self.d_idx)
         if xf.dtype != torch.float32:
             xf = xf.float()
-        if self.up._forward_pre_hooks or self.up._forward_hooks:
-            h = self.up(self.cdf(xf))  # hooks (e.g. a BucketTracker) see up's input, as in the reference
+        if _observed(self.up):
+            h = self.up(self.cdf(xf))  # a BucketTracker (hook or counting forward) sees up's input, as in the reference
         else:
             ln = self.cdf.ln
             h = _FnV2.apply(xf, ln.weight, ln.bias, ln.eps, self.up.table, self.up.bias, self.up.bw)
