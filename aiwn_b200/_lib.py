@@ -79,6 +79,8 @@ def load():
         lib.il_allreduce_scratch_bytes.restype = i64
         lib.il_allreduce_sum.argtypes = [vp, vp, i64, ci, ci, f64, f64, vp]
         lib.il_allreduce_sum.restype = ci
+        lib.il_allreduce_sum_noalloc.argtypes = [vp, i64, ci, f64, vp]
+        lib.il_allreduce_sum_noalloc.restype = ci
         lib.il_kernel_launches.argtypes = []
         lib.il_kernel_launches.restype = i64
         lib.il_check_device_status.argtypes = [vp]

@@ -321,6 +321,61 @@ __global__ void __launch_bounds__(kArThreads) allreduce_ll_kernel(const ArLLArgs
     }
 }
 
+// ---- variant for callers that cannot allocate: scratch in a static array ----
+//
+// One process drives every rank's GPU and launches all ranks of a call.  The
+// scratch is each device's own copy of a file-scope array, touched only by
+// that device: a device's static data is not mapped into its peers, so every
+// cross-device access goes to the callers' buffers (their allocations are,
+// with peer access enabled).  Rank p sums every rank's buffer into its
+// scratch (peer loads, ranks added in rank order, so every rank ends with
+// the same bits); after every rank has done so -- the host orders the
+// devices' streams with events, no device waits on another -- it copies the
+// scratch into its buffer.
+struct NaArgs {
+    const float* bufs[kArMaxRanks];  // every rank's buffer (the callers' allocations)
+    float* scratch;                  // this device's copy of the static array
+    int64_t n;
+    int world;
+    float scale;
+};
+
+__global__ void __launch_bounds__(kArThreads) allreduce_noalloc_sum_kernel(const NaArgs a) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t n4 = a.n / 4;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+        float4 s = __ldcg(reinterpret_cast<const float4*>(a.bufs[0]) + i);
+        for (int q = 1; q < a.world; ++q) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(a.bufs[q]) + i);
+            s.x += v.x;
+            s.y += v.y;
+            s.z += v.z;
+            s.w += v.w;
+        }
+        s.x *= a.scale;
+        s.y *= a.scale;
+        s.z *= a.scale;
+        s.w *= a.scale;
+        reinterpret_cast<float4*>(a.scratch)[i] = s;
+    }
+    const int64_t e = 4 * n4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // the n % 4 tail
+    if (e < a.n && blockIdx.x == 0) {
+        float s = __ldcg(a.bufs[0] + e);
+        for (int q = 1; q < a.world; ++q) s += __ldcg(a.bufs[q] + e);
+        a.scratch[e] = s * a.scale;
+    }
+}
+
+__global__ void __launch_bounds__(kArThreads) allreduce_noalloc_copy_kernel(float* buf, const float* scratch,
+                                                                             int64_t n) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t n4 = n / 4;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride)
+        reinterpret_cast<float4*>(buf)[i] = reinterpret_cast<const float4*>(scratch)[i];
+    const int64_t e = 4 * n4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e < n && blockIdx.x == 0) buf[e] = scratch[e];
+}
+
 struct ArPlan {
     int blocks = 1;
     int64_t chunk4 = 0;

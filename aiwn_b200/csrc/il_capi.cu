@@ -221,6 +221,88 @@ int attn_launch(Kern kern, int64_t smem, int64_t B, int64_t T, int64_t H, cudaSt
     return launch_status();
 }
 
+// ---- all-reduce without allocation (il_allreduce_sum_noalloc) -------------
+//
+// The sum is built in this file-scope array: every GPU that loads the library
+// holds one copy (kNoAllocMaxElems floats, 1 MiB) until the process exits, and
+// only that GPU touches it.  In host code the name is only a stand-in for the
+// device copies; their addresses come from cudaGetSymbolAddress with each
+// device current, once per device, on the first call that uses the device,
+// which also enables peer access between the call's devices and creates the
+// two events per device that order the devices' streams.  Nothing in the
+// array has to start at zero: every call overwrites the elements it reads.
+constexpr int64_t kNoAllocMaxElems = (int64_t)1 << 18;  // fp32 elements per buffer
+constexpr int kNoAllocMaxRanks = 8;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocMaxElems];
+
+struct NoAllocDev {
+    float* scratch = nullptr;               // this device's copy (set-up done when non-null)
+    cudaEvent_t entered = nullptr, summed = nullptr;
+    bool peer[kMaxDevices] = {};
+};
+NoAllocDev g_noalloc[kMaxDevices];
+std::mutex g_noalloc_mu;
+
+// addresses of the devices' copies, events, peer access between devices 0..world-1
+int noalloc_setup(int world) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    for (int p = 0; p < world; ++p) {
+        NoAllocDev& d = g_noalloc[p];
+        if (cudaSetDevice(p) != cudaSuccess) {
+            cudaGetLastError();
+            return IL_ERR_DEVICE;
+        }
+        if (!d.scratch) {
+            void* ptr = nullptr;
+            if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) {
+                cudaGetLastError();
+                return IL_ERR_DEVICE;
+            }
+            if (cudaEventCreateWithFlags(&d.entered, cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&d.summed, cudaEventDisableTiming) != cudaSuccess) {
+                cudaGetLastError();
+                return IL_ERR_LAUNCH;
+            }
+            d.scratch = static_cast<float*>(ptr);
+        }
+        for (int q = 0; q < world; ++q) {
+            if (q == p || d.peer[q]) continue;
+            int can = 0;
+            if (cudaDeviceCanAccessPeer(&can, p, q) != cudaSuccess || !can) {
+                cudaGetLastError();
+                return IL_ERR_DEVICE;
+            }
+            const cudaError_t e = cudaDeviceEnablePeerAccess(q, 0);
+            if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) {
+                cudaGetLastError();
+                return IL_ERR_DEVICE;
+            }
+            cudaGetLastError();  // clears cudaErrorPeerAccessAlreadyEnabled
+            d.peer[q] = true;
+        }
+    }
+    return IL_OK;
+}
+
+// every stream of the call waits for every other device's event (recorded
+// just before); the host orders the devices, no kernel waits on another
+int noalloc_cross_wait(int world, void* const* streams, bool summed) {
+    for (int p = 0; p < world; ++p) {
+        if (cudaSetDevice(p) != cudaSuccess) return IL_ERR_DEVICE;
+        if (cudaEventRecord(summed ? g_noalloc[p].summed : g_noalloc[p].entered, (cudaStream_t)streams[p]) !=
+            cudaSuccess)
+            return IL_ERR_LAUNCH;
+    }
+    for (int p = 0; p < world; ++p) {
+        if (cudaSetDevice(p) != cudaSuccess) return IL_ERR_DEVICE;
+        for (int q = 0; q < world; ++q)
+            if (q != p && cudaStreamWaitEvent((cudaStream_t)streams[p],
+                                              summed ? g_noalloc[q].summed : g_noalloc[q].entered, 0) != cudaSuccess)
+                return IL_ERR_LAUNCH;
+    }
+    return IL_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -683,6 +765,61 @@ int il_allreduce_sum(float* const* bufs, void* const* scratch, int64_t n, int ra
     a.timeout_ns = tns;
     il::launch_allreduce(a, pl, s);
     return launch_status();
+}
+
+int il_allreduce_sum_noalloc(float* const* bufs, int64_t n, int world, double scale, void* const* streams) {
+    if (world < 1 || world > kNoAllocMaxRanks || n < 0 || n > kNoAllocMaxElems) return IL_ERR_SHAPE;
+    if (!(scale == scale)) return IL_ERR_VALUE;
+    if (!bufs || !streams) return IL_ERR_NULL;
+    for (int p = 0; p < world; ++p) {
+        if (!bufs[p]) return IL_ERR_NULL;
+        if ((uintptr_t)bufs[p] & 15) return IL_ERR_ALIGN;
+    }
+    if (n == 0) return IL_OK;
+    int caller = 0, ndev = 0;
+    if (cudaGetDevice(&caller) != cudaSuccess || cudaGetDeviceCount(&ndev) != cudaSuccess) {
+        cudaGetLastError();
+        return IL_ERR_DEVICE;
+    }
+    if (world > ndev) return IL_ERR_SHAPE;
+    int st = noalloc_setup(world);
+    // every rank's buffer is final (and the previous call's copies are done) ...
+    if (st == IL_OK) st = noalloc_cross_wait(world, streams, false);
+    // ... each device sums every buffer into its own scratch ...
+    for (int p = 0; p < world && st == IL_OK; ++p) {
+        if (cudaSetDevice(p) != cudaSuccess) {
+            st = IL_ERR_DEVICE;
+            break;
+        }
+        int sms = 0;
+        if ((st = check_device(&sms))) break;
+        il::NaArgs a;
+        memset(&a, 0, sizeof(a));
+        for (int q = 0; q < world; ++q) a.bufs[q] = bufs[q];
+        a.scratch = g_noalloc[p].scratch;
+        a.n = n;
+        a.world = world;
+        a.scale = (float)scale;
+        il::allreduce_noalloc_sum_kernel<<<grid_for((n + 3) / 4, il::kArThreads, sms), il::kArThreads, 0,
+                                           (cudaStream_t)streams[p]>>>(a);
+        st = launch_status();
+    }
+    // ... and once every device has read every buffer, copies its sum in
+    if (st == IL_OK) st = noalloc_cross_wait(world, streams, true);
+    for (int p = 0; p < world && st == IL_OK; ++p) {
+        if (cudaSetDevice(p) != cudaSuccess) {
+            st = IL_ERR_DEVICE;
+            break;
+        }
+        int sms = 0;
+        if ((st = check_device(&sms))) break;
+        il::allreduce_noalloc_copy_kernel<<<grid_for((n + 3) / 4, il::kArThreads, sms), il::kArThreads, 0,
+                                            (cudaStream_t)streams[p]>>>(bufs[p], g_noalloc[p].scratch, n);
+        st = launch_status();
+    }
+    cudaGetLastError();
+    cudaSetDevice(caller);
+    return st;
 }
 
 int64_t il_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }

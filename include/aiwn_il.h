@@ -241,6 +241,29 @@ IL_API int il_allreduce_sum(float* const* bufs, void* const* scratch, int64_t n,
                             double scale, double timeout_s, void* stream);
 
 /*
+ * il_allreduce_sum for callers that cannot allocate device memory: no
+ * counterpart in the reference.  Meant for code that drives all the GPUs of
+ * a node from one process but may not call cudaMalloc itself -- for example
+ * a plugin inside a host framework whose memory pool owns every byte of the
+ * device, or code running where an allocation would stall or fail -- and so
+ * cannot provide the scratch region il_allreduce_sum needs.  One call sums
+ * bufs[0..world-1] in place (times scale): bufs[p] is a 16-byte aligned
+ * device pointer on device p (host array), streams[p] a stream of device p;
+ * the call enqueues every device's work itself and orders the devices'
+ * streams with events (no kernel waits on another).  Each device builds the
+ * sum in a static array compiled into the library (1 MiB, held by every GPU
+ * that loads it until the process exits), then copies it into its buffer;
+ * hence n <= 2^18 elements and world <= 8 (devices 0..world-1), IL_ERR_SHAPE
+ * beyond.  The first call that uses a device looks up that device's copy,
+ * creates its two events and enables peer access between the call's devices
+ * (no allocation of device memory), so make it before any stream capture.
+ * All calls share the static arrays, so calls whose kernels overlap on the
+ * GPUs race: order them (the same streams, or synchronise between calls).
+ */
+IL_API int il_allreduce_sum_noalloc(float* const* bufs, int64_t n, int world, double scale,
+                                    void* const* streams);
+
+/*
  * Number of kernels this library has launched in the process so far
  * (host-side counter, all devices and threads).  Lets a caller count the
  * library's launches inside a timed region.
