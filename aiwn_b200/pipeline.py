@@ -20,11 +20,57 @@ same as for device tensors.
 """
 from __future__ import annotations
 
+import os
 import time
 
 import torch
 
 from . import _lib
+
+
+def _parse_cpulist(text: str) -> set:
+    cpus = set()
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        if "-" in part:
+            a, b = part.split("-")
+            cpus.update(range(int(a), int(b) + 1))
+        else:
+            cpus.add(int(part))
+    return cpus
+
+
+def gpu_numa_cpus(device) -> tuple:
+    """(NUMA node, CPUs local to it) of a CUDA device's PCI slot, from sysfs;
+    (None, None) where the platform does not say."""
+    dev = torch.device(device)
+    props = torch.cuda.get_device_properties(dev.index if dev.index is not None else torch.cuda.current_device())
+    addr = f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+    base = os.path.join("/sys/bus/pci/devices", addr)
+    try:
+        with open(os.path.join(base, "numa_node")) as f:
+            node = int(f.read().strip())
+        with open(os.path.join(base, "local_cpulist")) as f:
+            cpus = _parse_cpulist(f.read())
+    except (OSError, ValueError):
+        return None, None
+    return (node if node >= 0 else None), (cpus or None)
+
+
+def bind_host_to_gpu(device) -> dict:
+    """Restrict this process's host threads to the CPUs of the GPU's NUMA
+    node, so that pinned host buffers allocated afterwards (first touch) and
+    the threads that issue copies sit next to the GPU's PCIe root, and ranks
+    of a multi-GPU job spread over the sockets instead of all running on the
+    first.  Returns what it did (for the record)."""
+    node, cpus = gpu_numa_cpus(device)
+    allowed = os.sched_getaffinity(0)
+    use = (cpus & allowed) if cpus else None
+    if use:
+        os.sched_setaffinity(0, use)
+        torch.set_num_threads(max(1, min(torch.get_num_threads(), len(use))))
+    return {"numa_node": node, "cpus": len(use) if use else len(allowed), "bound": bool(use)}
 
 
 class HostPipeline:

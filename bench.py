@@ -778,9 +778,13 @@ def run_ours(args, cfg, world, rank, local):
         return run_ours_v2(args, cfg, world, rank, local)
     from aiwn_b200 import IndexedLinear, _lib
     from aiwn_b200.distributed import TokenParallelIndexedLinear
-    from aiwn_b200.pipeline import HostPipeline
+    from aiwn_b200.pipeline import HostPipeline, bind_host_to_gpu
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    # host threads and pinned buffers of the e2e leg next to this GPU (the CPU
+    # baseline legs below restore all CPUs)
+    cpus_all = os.sched_getaffinity(0)
+    numa = bind_host_to_gpu(dev)
     N, IN, OUT, K = cfg["B"] * cfg["seq"], cfg["IN"], cfg["OUT"], cfg["K"]
     bw = 2.0 / K
     sx = 2 if cfg["dtype"] == "bf16" else 4
@@ -936,9 +940,20 @@ def run_ours(args, cfg, world, rank, local):
     dom = ("forward", ms_fwd, b_fwd) if ms_fwd >= ms_bwd else ("backward", ms_bwd, b_bwd)
     achieved = dom[2] / (dom[1] * 1e-3) / 1e9
     traffic = None
+    onchip = None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tp):
-        traffic = json.load(open(tp)).get(f"{args.config}:{dom[0]}")
+        tj = json.load(open(tp))
+        traffic = tj.get(f"{args.config}:{dom[0]}")
+        wf = tj.get(f"{args.config}:{dom[0]}:lsu_wavefronts_per_sm")
+        if wf:
+            # the pipe that binds the kernel: L1 data-pipe wavefronts per SM (ncu)
+            # at one per SM clock, against the launch's CUDA-event time
+            mhz = (clk or {}).get("sm_mhz") or 1965.0
+            floor_us = wf / mhz
+            onchip = {"bound": "l1_data_pipe", "wavefronts_per_sm": wf, "sm_mhz": mhz, "floor_us": floor_us,
+                      "achieved_us": dom[1] * 1e3, "frac": floor_us / (dom[1] * 1e3),
+                      "source": "profiles/traffic.json (ncu l1tex__data_pipe_lsu_wavefronts, one launch)"}
     res = {
         "metric": METRIC,
         "value": world * N / (ms_step * 1e-3),
@@ -965,7 +980,7 @@ def run_ours(args, cfg, world, rank, local):
         },
         "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind,
-                     "algorithmic_bytes_per_launch": dom[2]},
+                     "algorithmic_bytes_per_launch": dom[2], "onchip_ceiling": onchip},
         "e2e": {"value": world * N / (ms_e2e * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": xh[0].numel() * xh[0].element_size() + goh[0].numel() * 4,
                 "d2h_bytes_per_step": N * OUT * 4 + gxh[0].numel() * gxh[0].element_size(),
@@ -976,6 +991,8 @@ def run_ours(args, cfg, world, rank, local):
         "gpu_launches": launches,
         "clocks": clk,
     }
+    res["e2e"]["host_binding"] = numa
+    os.sched_setaffinity(0, cpus_all)
     if world == 1 and not args.no_reference_gpu:
         res["reference_gpu"] = reference_gpu(cfg, xs[0], table, bias, gos[0])
         res["reference_triton"] = reference_triton(cfg, xs[0], table, bias, gos[0])
