@@ -363,6 +363,43 @@ def cpu_baseline(cfg, seconds=12.0):
                       f"oracle/eager_port.py) in {seconds:.0f} s on {cores} threads"}
 
 
+def host_copy_probe(dev, world, local, mib=16, reps=5):
+    """Pinned host <-> device copy rates of this rank (GB/s) for `mib`-MiB
+    copies, host to device alone, device to host alone and both at once, with
+    every rank copying at the same time (a barrier before each pattern): the
+    host-side limit of the end-to-end leg."""
+    n = mib * 2**20 // 4
+    h_src = torch.empty(n, dtype=torch.float32).pin_memory()
+    h_dst = torch.empty(n, dtype=torch.float32).pin_memory()
+    d_a = torch.empty(n, device=dev)
+    d_b = torch.empty(n, device=dev)
+    s_up, s_down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def sync():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier(device_ids=[local])
+
+    def timed(up, down):
+        sync()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            if up:
+                with torch.cuda.stream(s_up):
+                    d_a.copy_(h_src, non_blocking=True)
+            if down:
+                with torch.cuda.stream(s_down):
+                    h_dst.copy_(d_b, non_blocking=True)
+        torch.cuda.synchronize(dev)
+        return (time.perf_counter() - t0) / reps
+
+    timed(True, True)
+    nbytes = n * 4
+    t_up, t_down, t_both = timed(True, False), timed(False, True), timed(True, True)
+    return {"copy_mib": mib, "h2d_gbs": nbytes / t_up / 1e9, "d2h_gbs": nbytes / t_down / 1e9,
+            "both_gbs": 2 * nbytes / t_both / 1e9, "ranks_copying": world}
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -932,6 +969,7 @@ def run_ours(args, cfg, world, rank, local):
     e2e_reps = max(10, min(args.steps, 200))
     ms_e2e = time_calls(e2e_step, e2e_reps)
     clk = clocks.stop() if clocks else None
+    host_bw = host_copy_probe(dev, world, local)
 
     if rank != 0:
         return None
@@ -992,6 +1030,11 @@ def run_ours(args, cfg, world, rank, local):
         "clocks": clk,
     }
     res["e2e"]["host_binding"] = numa
+    res["e2e"]["host_copy_rates_rank0"] = host_bw
+    moved = res["e2e"]["h2d_bytes_per_step"] + res["e2e"]["d2h_bytes_per_step"]
+    # the step's copies alone at the rate measured with every rank copying both ways
+    res["e2e"]["copy_floor_ms"] = moved / (host_bw["both_gbs"] * 1e9) * 1e3
+    res["e2e"]["copy_floor_frac"] = res["e2e"]["copy_floor_ms"] / ms_e2e
     os.sched_setaffinity(0, cpus_all)
     if world == 1 and not args.no_reference_gpu:
         res["reference_gpu"] = reference_gpu(cfg, xs[0], table, bias, gos[0])
