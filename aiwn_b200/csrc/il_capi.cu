@@ -23,6 +23,7 @@
 #include "il_attn.cuh"
 #include "il_allreduce.cuh"
 #include "il_tc.cuh"
+#include "il_fwd_wide.cuh"
 
 namespace {
 
@@ -122,6 +123,17 @@ int forward_dispatch(const void* x, int x_dtype, const float* table, const float
             return launch_status();
         }
     }
+    // AIWN_IL_FORWARD=wide: the warp-per-token forward wherever it applies
+    if (fv && strcmp(fv, "wide") == 0 && il::fast_forward_args_ok(x, x_dtype, table, bias, out, N, IN, OUT, c.K, c)) {
+        const int rc = il::wide_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s);
+        if (rc != il::kNotApplicable) {
+            if (rc) {
+                cudaGetLastError();
+                return IL_ERR_LAUNCH;
+            }
+            return launch_status();
+        }
+    }
     const KernelChoice path = kernel_choice("AIWN_IL_FORWARD", "token", "cluster");
     // Rows of a multiple of 32 outputs over few bins (K <= 64): the cluster
     // kernel's lanes read consecutive chunks of one table row, and it beat the
@@ -148,6 +160,18 @@ int forward_dispatch(const void* x, int x_dtype, const float* table, const float
     }
     if (path != kOnlyOther && il::fast_forward_args_ok(x, x_dtype, table, bias, out, N, IN, OUT, c.K, c)) {
         const int rc = il::token_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s);
+        if (rc != il::kNotApplicable) {
+            if (rc) {
+                cudaGetLastError();
+                return IL_ERR_LAUNCH;
+            }
+            return launch_status();
+        }
+    }
+    if (path == kAny && il::fast_forward_args_ok(x, x_dtype, table, bias, out, N, IN, OUT, c.K, c)) {
+        // tables too large to keep resident, rows of a multiple of 128 outputs
+        // over at most 128 bins: one warp per token streams the table
+        const int rc = il::wide_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s);
         if (rc != il::kNotApplicable) {
             if (rc) {
                 cudaGetLastError();

@@ -363,11 +363,11 @@ def cpu_baseline(cfg, seconds=12.0):
                       f"oracle/eager_port.py) in {seconds:.0f} s on {cores} threads"}
 
 
-def host_copy_probe(dev, world, local, mib=16, reps=5):
+def host_copy_probe(dev, world, local, mib=32, reps=4, trials=3):
     """Pinned host <-> device copy rates of this rank (GB/s) for `mib`-MiB
     copies, host to device alone, device to host alone and both at once, with
-    every rank copying at the same time (a barrier before each pattern): the
-    host-side limit of the end-to-end leg."""
+    every rank copying at the same time (a barrier before each pattern), the
+    best of `trials`: the host-side limit of the end-to-end leg."""
     n = mib * 2**20 // 4
     h_src = torch.empty(n, dtype=torch.float32).pin_memory()
     h_dst = torch.empty(n, dtype=torch.float32).pin_memory()
@@ -395,7 +395,9 @@ def host_copy_probe(dev, world, local, mib=16, reps=5):
 
     timed(True, True)
     nbytes = n * 4
-    t_up, t_down, t_both = timed(True, False), timed(False, True), timed(True, True)
+    t_up = min(timed(True, False) for _ in range(trials))
+    t_down = min(timed(False, True) for _ in range(trials))
+    t_both = min(timed(True, True) for _ in range(trials))
     return {"copy_mib": mib, "h2d_gbs": nbytes / t_up / 1e9, "d2h_gbs": nbytes / t_down / 1e9,
             "both_gbs": 2 * nbytes / t_both / 1e9, "ranks_copying": world}
 
@@ -880,11 +882,33 @@ def run_ours(args, cfg, world, rank, local):
 
     clocks = ClockSampler(local) if rank == 0 else None
 
+    # The timed calls replay CUDA graphs, one per input set, captured from the
+    # same library calls: a small layer's kernels run for less time than one
+    # Python call takes to check and enqueue them, so eager timing would
+    # measure the host.  The NCCL exchange stays eager (no NCCL in graphs).
+    use_graphs = peer is not None or world == 1
+
+    def graphed(fn):
+        if not use_graphs:
+            return fn, None
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            fn(0)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        graphs, l0 = [], _lib.kernel_launches()
+        for k in range(n_sets):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn(k)
+            graphs.append(g)
+        per_call = (_lib.kernel_launches() - l0) / n_sets
+        return (lambda k: graphs[k % n_sets].replay()), per_call
+
     for k in range(max(3, args.warmup)):
         step(k)
     sync_all()
-    if clocks:
-        clocks.start()
     launches0 = _lib.kernel_launches()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sync_all()
@@ -893,8 +917,23 @@ def run_ours(args, cfg, world, rank, local):
         step(k)
     ev1.record()
     sync_all()
-    launches = _lib.kernel_launches() - launches0
+    eager_launches = _lib.kernel_launches() - launches0
+    ms_step_eager = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+
+    step_g, step_launches = graphed(step)
+    for k in range(max(3, args.warmup)):
+        step_g(k)
+    sync_all()
+    if clocks:
+        clocks.start()
+    sync_all()
+    ev0.record()
+    for k in range(args.steps):
+        step_g(k)
+    ev1.record()
+    sync_all()
     ms_step = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    launches = int(round(step_launches * args.steps)) if step_launches is not None else eager_launches
 
     # per-call device time of the forward and of the backward (same stream)
     def time_calls(fn, reps):
@@ -908,9 +947,11 @@ def run_ours(args, cfg, world, rank, local):
         return max_over_ranks(e0.elapsed_time(e1) / reps)
 
     reps = max(args.steps, 20)
-    ms_fwd = time_calls(lambda k: _lib.forward(xs[k % n_sets], table, bias, outs[k % n_sets], bw), reps)
-    ms_bwd = time_calls(lambda k: _lib.backward(gos[k % n_sets], xs[k % n_sets], table, gxs[k % n_sets],
-                                                gt, gb, bw, ws if ws_n else None), reps)
+    fwd_g, _ = graphed(lambda k: _lib.forward(xs[k % n_sets], table, bias, outs[k % n_sets], bw))
+    bwd_g, _ = graphed(lambda k: _lib.backward(gos[k % n_sets], xs[k % n_sets], table, gxs[k % n_sets],
+                                               gt, gb, bw, ws if ws_n else None))
+    ms_fwd = time_calls(fwd_g, reps)
+    ms_bwd = time_calls(bwd_g, reps)
 
     # training step with the fused Adam update of table and bias
     m_t, v_t = torch.zeros_like(bucket), torch.zeros_like(bucket)
@@ -921,6 +962,7 @@ def run_ours(args, cfg, world, rank, local):
         _lib.adam_step(params, bucket, m_t, v_t, 1e-3, 0.9, 0.999, 1e-8, k + 1)
 
     ms_train = time_calls(train_step, reps)
+    del step_g, fwd_g, bwd_g
 
     # the same step without the gradient all-reduce (multi-GPU runs): the
     # difference is the exchange step's cost
@@ -930,7 +972,9 @@ def run_ours(args, cfg, world, rank, local):
             i = k % n_sets
             _lib.forward(xs[i], table, bias, outs[i], bw)
             _lib.backward(gos[i], xs[i], table, gxs[i], gt, gb, bw, ws if ws_n else None)
-        ms_noar = time_calls(step_local, reps)
+        local_g, _ = graphed(step_local)
+        ms_noar = time_calls(local_g, reps)
+        del local_g
         if peer is not None:
             # the same step with NCCL's all-reduce of a plain bucket, for comparison
             nb = torch.empty_like(bucket)
@@ -1007,10 +1051,14 @@ def run_ours(args, cfg, world, rank, local):
         "fwd_tokens_per_s": world * N / (ms_fwd * 1e-3),
         "fwd_bwd_tokens_per_s": world * N / (ms_step * 1e-3),
         "train_step_tokens_per_s": world * N / (ms_train * 1e-3),
-        "ms": {"fwd": ms_fwd, "bwd": ms_bwd, "fwd_bwd": ms_step, "train_step_adam": ms_train},
+        "ms": {"fwd": ms_fwd, "bwd": ms_bwd, "fwd_bwd": ms_step, "train_step_adam": ms_train,
+               "fwd_bwd_eager": ms_step_eager},
+        "timing": ("CUDA-graph replays of the library calls, one graph per input set; fwd_bwd_eager: "
+                   "the same calls from Python" if use_graphs else "eager library calls"),
         **({"fwd_bwd_without_allreduce": {"tokens_per_s": world * N / (ms_noar * 1e-3), "ms": ms_noar}}
            if ms_noar is not None else {}),
-        **({"fwd_bwd_nccl_allreduce": {"tokens_per_s": world * N / (ms_nccl * 1e-3), "ms": ms_nccl}}
+        **({"fwd_bwd_nccl_allreduce": {"tokens_per_s": world * N / (ms_nccl * 1e-3), "ms": ms_nccl,
+                                        "timing": "eager (compare with ms.fwd_bwd_eager)"}}
            if ms_nccl is not None else {}),
         "hbm_roofline_frac": {
             "fwd": b_fwd / (ms_fwd * 1e-3) / 1e9 / hbm,

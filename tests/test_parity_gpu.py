@@ -108,16 +108,68 @@ def test_tensor_core_forward_nonfinite_and_partial_tile(monkeypatch):
     normwise_close(out.cpu().numpy(), ref, FWD_RTOL["f32"], "tc non-finite")
 
 
-def test_c4_parity_at_the_bench_launch_size():
+@pytest.mark.parametrize("fwd", ["auto", "token"], ids=["wide_fwd", "stream_fwd"])
+def test_c4_parity_at_the_bench_launch_size(fwd, monkeypatch):
     """The large-table configuration at the size one GPU runs in the bench:
     16384 tokens, in_d = out_d = 1024, K = 64, x = clamp(N(0, 0.5), -1, 1).
-    Exercises the streamed forward's multi-tile path and the sorted backward's
-    128-column j-ranges with atomically added dx at that launch shape; every
-    output and gradient is compared with the oracle."""
+    Exercises the forward that the library picks there (one warp per token,
+    streamed table) and the streamed per-lane forward (AIWN_IL_FORWARD=token
+    falls through to it), and the sorted backward's 128-column j-ranges with
+    atomically added dx at that launch shape; every output and gradient is
+    compared with the oracle."""
     from il_cases import Case
+    monkeypatch.setenv("AIWN_IL_FORWARD", fwd)
     c = Case("c4_bench_launch", 16384, 1024, 1024, 64, "clamp_normal", "f32", 0.1, 40)
     x, table, bias, go = make_inputs(c)
     check_against_oracle(c, x, table, bias, go)
+
+
+def _wide_cases():
+    from il_cases import Case
+    listed = [c for c in CASES + EDGE_CASES if c.OUT % 128 == 0 and c.K <= 128 and (c.K & (c.K - 1)) == 0]
+    return listed + [
+        Case("wide_in1020_out128_k64", 333, 1020, 128, 64, "wide", "f32", 0.3, 41),  # entry-block tail
+        Case("wide_in9_out384_k128", 1000, 9, 384, 128, "wide", "f32", 0.3, 42),     # one column per stage
+        Case("wide_in24_out128_k16_bf16", 2049, 24, 128, 16, "wide", "bf16", 0.3, 43),
+        Case("wide_in1_out128_k2", 5, 1, 128, 2, "wide", "f32", 0.3, 44),
+        Case("wide_in64_out256_k32_n7000", 7000, 64, 256, 32, "clamp_normal", "f32", 0.3, 45),
+    ]
+
+
+@pytest.mark.parametrize("c", _wide_cases(), ids=lambda c: c.name)
+def test_wide_forward_vs_oracle(c, monkeypatch):
+    """The warp-per-token forward (out_d a multiple of 128, K <= 128), pinned
+    with AIWN_IL_FORWARD=wide: partial token tiles, entry blocks past in_d,
+    1..8 input columns per stage, bf16 x."""
+    monkeypatch.setenv("AIWN_IL_FORWARD", "wide")
+    x, table, bias, _ = make_inputs(c)
+    out = torch.empty(c.N, c.OUT, device=DEV)
+    _lib.forward(x.to(DEV), table.to(DEV), bias.to(DEV), out, 2.0 / c.K)
+    ref = oracle.forward(x_numpy(x), table.numpy(), bias.numpy(), 2.0 / c.K, x_dtype=c.dtype)
+    normwise_close(out.cpu().numpy(), ref, FWD_RTOL[c.dtype], f"{c.name} out (wide)")
+
+
+def test_wide_forward_matches_streamed_forward_bitwise(monkeypatch):
+    """Same products in the same order: the warp-per-token forward and the
+    streamed per-lane forward give identical bits, non-finite inputs included."""
+    g = torch.Generator().manual_seed(9)
+    N, IN, OUT, K = 1500, 40, 256, 64
+    x = torch.rand(N, IN, generator=g) * 2.4 - 1.2
+    x[3, 1] = float("inf")
+    x[4, 0] = float("-inf")
+    x[7, 5] = float("nan")
+    table = (torch.randn(K, IN, OUT, generator=g) / math.sqrt(IN)).to(DEV)
+    bias = (torch.randn(OUT, generator=g) * 0.1).to(DEV)
+    xd = x.to(DEV)
+    outs = {}
+    for path in ("wide", "token"):
+        monkeypatch.setenv("AIWN_IL_FORWARD", path)
+        outs[path] = torch.empty(N, OUT, device=DEV)
+        _lib.forward(xd, table, bias, outs[path], 2.0 / K)
+    a, b = outs["wide"].cpu().numpy(), outs["token"].cpu().numpy()
+    assert same_bits(a, b)
+    ref = oracle.forward(x.numpy(), table.cpu().numpy(), bias.cpu().numpy(), 2.0 / K)
+    normwise_close(a, ref, FWD_RTOL["f32"], "wide non-finite")
 
 
 @pytest.mark.parametrize("name", case_names())
