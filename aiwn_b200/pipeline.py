@@ -81,19 +81,30 @@ class HostPipeline:
     whole batch fits ``max_resident_bytes``; then the only ordering between
     chunks is that of each stream, and the upload of chunk c+1 never waits for
     chunk c's results to leave.  Larger batches reuse a ring of slots.
+
+    Uploads can be coarser than the compute chunks (``pieces`` < ``chunks``,
+    resident batches only): host-to-device copies of a few MiB run well
+    below the copy engine's rate for large ones on some hosts, while the
+    kernels and the downloads gain from fine chunks.  A chunk then waits for
+    the upload piece that holds its tokens.
     """
 
-    # chunk counts tried when none is given
+    # chunk counts and upload pieces tried when none is given
     TUNE_CHUNKS = (1, 2, 4, 8, 16)
+    TUNE_PIECES = (1, 2, 4)
     TUNE_MIN_CHUNK = 4096  # tokens
 
     def __init__(self, layer, chunks: int | None = None, device=None, graphs: bool = True,
-                 max_resident_bytes: int = 1 << 30):
+                 max_resident_bytes: int = 1 << 30, pieces: int | None = None):
         self.layer = layer
         inner = getattr(layer, "layer", layer)
         self.inner = inner
         self.auto = chunks is None
         self.chunks = 1 if chunks is None else max(1, int(chunks))
+        # upload pieces: one per chunk unless given (must divide the chunk count)
+        self.pieces = self.chunks if pieces is None else max(1, min(int(pieces), self.chunks))
+        if self.chunks % self.pieces:
+            raise ValueError(f"pieces ({self.pieces}) must divide chunks ({self.chunks})")
         self._tuned = {}  # (N, in, out, x dtype) -> tuned HostPipeline
         self.device = torch.device(device) if device is not None else inner.table.device
         self.s_h2d = torch.cuda.Stream(self.device)
@@ -112,14 +123,22 @@ class HostPipeline:
             xs = torch.empty(0, dtype=xdtype).element_size()
             slot_bytes = n * (2 * IN * xs + 2 * OUT * 4)
             nslots = max(2, min(self.chunks, self.max_resident_bytes // max(slot_bytes, 1)))
-            slots = [dict(x=mk(n, IN, dt=xdtype), go=mk(n, OUT), out=mk(n, OUT), gx=mk(n, IN, dt=xdtype))
-                     for _ in range(nslots)]
+            if nslots >= self.chunks:
+                # resident: one buffer per kind, chunk c is rows [c*n, (c+1)*n),
+                # so that an upload piece can span several chunks
+                full = dict(x=mk(self.chunks * n, IN, dt=xdtype), go=mk(self.chunks * n, OUT),
+                            out=mk(self.chunks * n, OUT), gx=mk(self.chunks * n, IN, dt=xdtype))
+                slots = [{k: v[c * n:(c + 1) * n] for k, v in full.items()} for c in range(self.chunks)]
+            else:
+                slots = [dict(x=mk(n, IN, dt=xdtype), go=mk(n, OUT), out=mk(n, OUT), gx=mk(n, IN, dt=xdtype))
+                         for _ in range(nslots)]
+                full = None
             K = self.inner.K
             # the gradients of all chunks add up here (il_backward_accumulate)
             grads = dict(gt_sum=mk(K, IN, OUT), gb_sum=mk(OUT))
-            self._bufs = (key, slots, grads)
+            self._bufs = (key, slots, grads, full)
             self._graph_cache.clear()
-        return self._bufs[1], self._bufs[2]
+        return self._bufs[1], self._bufs[2], self._bufs[3]
 
     def _issue(self, x_host, go_host, out_host, gx_host, table, bias, want_grads):
         """Enqueue the whole pipelined step; joins every side stream back into
@@ -128,8 +147,10 @@ class HostPipeline:
         N, IN = x_host.shape
         OUT, K = inner.out_dim, inner.K
         n = (N + self.chunks - 1) // self.chunks
-        slots, gr = self._buffers(n, IN, OUT, x_host.dtype)
+        slots, gr, full = self._buffers(n, IN, OUT, x_host.dtype)
         S = len(slots)
+        # upload pieces of cpp chunks each (resident buffers only)
+        cpp = self.chunks // self.pieces if full is not None else 1
         ws_n = _lib.workspace_bytes(n, IN, OUT, K, _lib.x_dtype_code(slots[0]["x"]))
         if ws_n and (self._ws is None or self._ws.numel() < ws_n):
             self._ws = torch.empty(ws_n, dtype=torch.uint8, device=self.device)
@@ -148,23 +169,31 @@ class HostPipeline:
                 break
             m = b - a
             sl = slots[c % S]
-            for lst in (x_up, go_up, fwd_done, bwd_done, out_down, gx_down):
+            for lst in (fwd_done, bwd_done, out_down, gx_down):
                 lst.append(ev())
-            with torch.cuda.stream(self.s_h2d):
-                if c >= S:
-                    self.s_h2d.wait_event(bwd_done[c - S])  # the slot's inputs are consumed
-                sl["x"][:m].copy_(x_host[a:b], non_blocking=True)
-                x_up[c].record(self.s_h2d)
-                sl["go"][:m].copy_(go_host[a:b], non_blocking=True)
-                go_up[c].record(self.s_h2d)
+            if c % cpp == 0:
+                # the upload piece of chunks c .. c+cpp-1
+                pa, pb = a, min(N, (c + cpp) * n)
+                x_up.append(ev())
+                go_up.append(ev())
+                with torch.cuda.stream(self.s_h2d):
+                    if c >= S:
+                        self.s_h2d.wait_event(bwd_done[c - S])  # the slot's inputs are consumed
+                    dst = full if cpp > 1 else {"x": sl["x"][:m], "go": sl["go"][:m]}
+                    lo_ = pa if cpp > 1 else 0
+                    dst["x"][lo_:lo_ + pb - pa].copy_(x_host[pa:pb], non_blocking=True)
+                    x_up[-1].record(self.s_h2d)
+                    dst["go"][lo_:lo_ + pb - pa].copy_(go_host[pa:pb], non_blocking=True)
+                    go_up[-1].record(self.s_h2d)
+            piece = c // cpp
             with torch.cuda.stream(self.s_cmp):
                 xs, gos = sl["x"][:m], sl["go"][:m]
-                self.s_cmp.wait_event(x_up[c])
+                self.s_cmp.wait_event(x_up[piece])
                 if c >= S:
                     self.s_cmp.wait_event(out_down[c - S])  # the slot's out has left
                 _lib.forward(xs, table, bias, sl["out"][:m], inner.bw)
                 fwd_done[c].record(self.s_cmp)
-                self.s_cmp.wait_event(go_up[c])
+                self.s_cmp.wait_event(go_up[piece])
                 if c >= S:
                     self.s_cmp.wait_event(gx_down[c - S])
                 _lib.backward(gos, xs, table, sl["gx"][:m], gr["gt_sum"] if want_grads else None,
@@ -189,11 +218,12 @@ class HostPipeline:
         on the machine.  Each candidate runs one untimed and three timed
         steps (gradients stay in the pipeline's own sums)."""
         N = x_host.shape[0]
-        cands = [c for c in self.TUNE_CHUNKS if c == 1 or N // c >= self.TUNE_MIN_CHUNK]
+        cands = [(c, q) for c in self.TUNE_CHUNKS if c == 1 or N // c >= self.TUNE_MIN_CHUNK
+                 for q in sorted(set(self.TUNE_PIECES) | {c}) if q <= c and c % q == 0]
         best = None
-        for c in cands:
+        for c, q in cands:
             p = HostPipeline(self.layer, chunks=c, device=self.device, graphs=self.graphs,
-                             max_resident_bytes=self.max_resident_bytes)
+                             max_resident_bytes=self.max_resident_bytes, pieces=q)
             cur = torch.cuda.current_stream(self.device)
             p._run(x_host, go_host, out_host, gx_host, True)
             cur.synchronize()
@@ -238,6 +268,13 @@ class HostPipeline:
         if not self.auto:
             return {"all": self.chunks}
         return {k[0][0]: p.chunks for k, p in self._tuned.items()}
+
+    @property
+    def chosen_pieces(self) -> dict:
+        """Upload pieces in use per batch size N (the tuned ones when auto)."""
+        if not self.auto:
+            return {"all": self.pieces}
+        return {k[0][0]: p.pieces for k, p in self._tuned.items()}
 
     def _run(self, x_host, go_host, out_host, gx_host, want_grads: bool):
         """One pipelined step with this instance's chunk count; returns the

@@ -1071,7 +1071,8 @@ def run_ours(args, cfg, world, rank, local):
                 "h2d_bytes_per_step": xh[0].numel() * xh[0].element_size() + goh[0].numel() * 4,
                 "d2h_bytes_per_step": N * OUT * 4 + gxh[0].numel() * gxh[0].element_size(),
                 "api": "aiwn_b200.pipeline.HostPipeline over TokenParallelIndexedLinear: forward+backward "
-                       f"of pinned host x/go into pinned host out/dx, {pipe.chosen_chunks.get(N)} chunks "
+                       f"of pinned host x/go into pinned host out/dx, {pipe.chosen_chunks.get(N)} chunks, "
+                       f"{pipe.chosen_pieces.get(N)} upload pieces "
                        "(tuned on the first call) with copies overlapped, replayed as one CUDA graph "
                        "(+gradient all-reduce when N>1)"},
         "gpu_launches": launches,

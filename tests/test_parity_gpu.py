@@ -309,14 +309,17 @@ def test_backward_accumulate_adds_into_grads():
     normwise_close(gx_acc.cpu().numpy(), gx.cpu().numpy(), 1e-6, "dx of the chunks")
 
 
-@pytest.mark.parametrize("chunks,resident", [(5, True), (5, False), (None, True)],
-                         ids=["per_chunk_buffers", "slot_ring", "tuned_chunks"])
+@pytest.mark.parametrize("chunks,pieces,resident", [(5, None, True), (5, None, False), (None, None, True),
+                                                    (6, 2, True), (8, 1, True), (6, 3, False)],
+                         ids=["per_chunk_buffers", "slot_ring", "tuned_chunks", "pieces_of_3_chunks",
+                              "one_upload", "ring_ignores_pieces"])
 @pytest.mark.parametrize("graphs", [True, False])
-def test_host_pipeline_matches_whole_batch_call(graphs, chunks, resident):
+def test_host_pipeline_matches_whole_batch_call(graphs, chunks, pieces, resident):
     """HostPipeline (chunked, copies overlapped on three streams, replayed
     from a CUDA graph or issued eagerly; device buffers per chunk or a ring
-    of two reused slots) gives the same out / dx as one call on the whole
-    batch and the same summed grads."""
+    of two reused slots; uploads per chunk or in pieces of several chunks)
+    gives the same out / dx as one call on the whole batch and the same
+    summed grads."""
     from aiwn_b200.pipeline import HostPipeline
     c = CASES[2]
     x, table, bias, go = make_inputs(c)
@@ -329,7 +332,8 @@ def test_host_pipeline_matches_whole_batch_call(graphs, chunks, resident):
     xh, goh = x.pin_memory(), go.pin_memory()
     outh = torch.empty(N, c.OUT).pin_memory()
     gxh = torch.empty(N, c.IN).pin_memory()
-    pipe = HostPipeline(m, chunks=chunks, graphs=graphs, max_resident_bytes=(1 << 30) if resident else 1)
+    pipe = HostPipeline(m, chunks=chunks, graphs=graphs, max_resident_bytes=(1 << 30) if resident else 1,
+                        pieces=pieces)
     for _ in range(2):  # second call reuses the buffers (and the graph); grads accumulate
         pipe.forward_backward(xh, goh, outh, gxh)
     torch.cuda.synchronize()
@@ -340,3 +344,4 @@ def test_host_pipeline_matches_whole_batch_call(graphs, chunks, resident):
     normwise_close(m.bias.grad.cpu().numpy(), 2 * gb.cpu().numpy(), GRAD_RTOL, "pipeline gb")
     if chunks is None:
         assert pipe.chosen_chunks[N] in HostPipeline.TUNE_CHUNKS
+        assert pipe.chosen_chunks[N] % pipe.chosen_pieces[N] == 0
