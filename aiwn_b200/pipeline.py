@@ -82,11 +82,13 @@ class HostPipeline:
     chunks is that of each stream, and the upload of chunk c+1 never waits for
     chunk c's results to leave.  Larger batches reuse a ring of slots.
 
-    Uploads can be coarser than the compute chunks (``pieces`` < ``chunks``,
-    resident batches only): host-to-device copies of a few MiB run well
-    below the copy engine's rate for large ones on some hosts, while the
-    kernels and the downloads gain from fine chunks.  A chunk then waits for
-    the upload piece that holds its tokens.
+    Copies can be coarser than the compute chunks (``pieces`` < ``chunks``,
+    resident batches only): every pinned host<->device copy costs ~9 us of
+    copy-engine time beyond its bytes on the hosts measured (two 21 MiB
+    copies, one each way, took 0.46 ms; the same bytes in 16 pieces each
+    0.72 ms), while the kernels gain from fine chunks.  A piece of several
+    chunks is uploaded with one copy per input, its chunks' forwards run,
+    its out leaves with one copy while their backwards run, then its dx.
     """
 
     # chunk counts and upload pieces tried when none is given
@@ -162,51 +164,50 @@ class HostPipeline:
         for s in (self.s_h2d, self.s_cmp, self.s_d2h):
             s.wait_stream(cur)
         ev = lambda: torch.cuda.Event()  # noqa: E731
-        x_up, go_up, fwd_done, bwd_done, out_down, gx_down = [], [], [], [], [], []
-        for c in range(self.chunks):
-            a, b = c * n, min(N, (c + 1) * n)
-            if a >= b:
-                break
-            m = b - a
-            sl = slots[c % S]
-            for lst in (fwd_done, bwd_done, out_down, gx_down):
-                lst.append(ev())
-            if c % cpp == 0:
-                # the upload piece of chunks c .. c+cpp-1
-                pa, pb = a, min(N, (c + cpp) * n)
-                x_up.append(ev())
-                go_up.append(ev())
-                with torch.cuda.stream(self.s_h2d):
-                    if c >= S:
-                        self.s_h2d.wait_event(bwd_done[c - S])  # the slot's inputs are consumed
-                    dst = full if cpp > 1 else {"x": sl["x"][:m], "go": sl["go"][:m]}
-                    lo_ = pa if cpp > 1 else 0
-                    dst["x"][lo_:lo_ + pb - pa].copy_(x_host[pa:pb], non_blocking=True)
-                    x_up[-1].record(self.s_h2d)
-                    dst["go"][lo_:lo_ + pb - pa].copy_(go_host[pa:pb], non_blocking=True)
-                    go_up[-1].record(self.s_h2d)
-            piece = c // cpp
+        nch = (N + n - 1) // n  # non-empty chunks
+        npieces = (nch + cpp - 1) // cpp
+        # per piece (= per chunk when cpp == 1): x_up, go_up, fwd_done, bwd_done, out_down, gx_down
+        x_up, go_up, fwd_done, bwd_done, out_down, gx_down = ([ev() for _ in range(npieces)] for _ in range(6))
+        for q in range(npieces):
+            c0, c1 = q * cpp, min(nch, (q + 1) * cpp)
+            pa, pb = c0 * n, min(N, c1 * n)
+            if cpp > 1:  # resident: one copy per piece, straight into the whole-batch buffers
+                xq, goq, outq, gxq = (full[k][pa:pb] for k in ("x", "go", "out", "gx"))
+            else:
+                sl = slots[q % S]
+                xq, goq, outq, gxq = (sl[k][:pb - pa] for k in ("x", "go", "out", "gx"))
+            with torch.cuda.stream(self.s_h2d):
+                if q >= S:
+                    self.s_h2d.wait_event(bwd_done[q - S])  # the slot's inputs are consumed
+                xq.copy_(x_host[pa:pb], non_blocking=True)
+                x_up[q].record(self.s_h2d)
+                goq.copy_(go_host[pa:pb], non_blocking=True)
+                go_up[q].record(self.s_h2d)
+            # the piece's forwards first, so that its out leaves while the backwards run
             with torch.cuda.stream(self.s_cmp):
-                xs, gos = sl["x"][:m], sl["go"][:m]
-                self.s_cmp.wait_event(x_up[piece])
-                if c >= S:
-                    self.s_cmp.wait_event(out_down[c - S])  # the slot's out has left
-                _lib.forward(xs, table, bias, sl["out"][:m], inner.bw)
-                fwd_done[c].record(self.s_cmp)
-                self.s_cmp.wait_event(go_up[piece])
-                if c >= S:
-                    self.s_cmp.wait_event(gx_down[c - S])
-                _lib.backward(gos, xs, table, sl["gx"][:m], gr["gt_sum"] if want_grads else None,
-                              gr["gb_sum"] if want_grads else None, inner.bw, self._ws if ws_n else None,
-                              accumulate=True)
-                bwd_done[c].record(self.s_cmp)
+                self.s_cmp.wait_event(x_up[q])
+                if q >= S:
+                    self.s_cmp.wait_event(out_down[q - S])  # the slot's out has left
+                for c in range(c0, c1):
+                    a, b = (c - c0) * n, min(pb - pa, (c - c0 + 1) * n)
+                    _lib.forward(xq[a:b], table, bias, outq[a:b], inner.bw)
+                fwd_done[q].record(self.s_cmp)
+                self.s_cmp.wait_event(go_up[q])
+                if q >= S:
+                    self.s_cmp.wait_event(gx_down[q - S])
+                for c in range(c0, c1):
+                    a, b = (c - c0) * n, min(pb - pa, (c - c0 + 1) * n)
+                    _lib.backward(goq[a:b], xq[a:b], table, gxq[a:b], gr["gt_sum"] if want_grads else None,
+                                  gr["gb_sum"] if want_grads else None, inner.bw, self._ws if ws_n else None,
+                                  accumulate=True)
+                bwd_done[q].record(self.s_cmp)
             with torch.cuda.stream(self.s_d2h):
-                self.s_d2h.wait_event(fwd_done[c])
-                out_host[a:b].copy_(sl["out"][:m], non_blocking=True)
-                out_down[c].record(self.s_d2h)
-                self.s_d2h.wait_event(bwd_done[c])
-                gx_host[a:b].copy_(sl["gx"][:m], non_blocking=True)
-                gx_down[c].record(self.s_d2h)
+                self.s_d2h.wait_event(fwd_done[q])
+                out_host[pa:pb].copy_(outq, non_blocking=True)
+                out_down[q].record(self.s_d2h)
+                self.s_d2h.wait_event(bwd_done[q])
+                gx_host[pa:pb].copy_(gxq, non_blocking=True)
+                gx_down[q].record(self.s_d2h)
         for s in (self.s_h2d, self.s_cmp, self.s_d2h):
             cur.wait_stream(s)
         return gr
