@@ -789,7 +789,16 @@ int il_allreduce_sum(float* const* bufs, void* const* scratch, int64_t n, int ra
         a.world = world;
         a.scale = (float)scale;
         a.timeout_ns = tns;
-        il::launch_allreduce_ll(a, il::ll_blocks(a.pairs, sms), s);
+        // one warp per (32 pairs, rank) at 4 and 8 ranks, one thread per pair
+        // otherwise; AIWN_IL_ALLREDUCE=warp|thread picks one (warp: 2, 4, 8 ranks)
+        const char* av = getenv("AIWN_IL_ALLREDUCE");
+        const bool warp = av && strcmp(av, "warp") == 0   ? il::ll_warp_ok(world)
+                          : av && strcmp(av, "thread") == 0 ? false
+                                                            : il::ll_warp_default(world);
+        if (warp)
+            il::launch_allreduce_ll_warp(a, il::ll_warp_blocks(a.pairs, world, sms), s);
+        else
+            il::launch_allreduce_ll(a, il::ll_blocks(a.pairs, sms), s);
         return launch_status();
     }
     il::ArArgs a;

@@ -1,8 +1,9 @@
 """Multi-GPU paths on real GPUs: one process per GPU, NCCL, two ranks.
 
 * the library's peer-memory all-reduce (il_allreduce_sum over torch
-  symmetric memory) against NCCL's all_reduce: odd sizes, repeated calls,
-  scaling, CUDA-graph replay; every rank ends with the same bits;
+  symmetric memory, both flag-in-word kernels) against NCCL's all_reduce:
+  odd sizes, repeated calls, scaling, CUDA-graph replay; every rank ends
+  with the same bits;
 * TokenParallelIndexedLinear with either exchange ("peer", "nccl") against
   the oracle on the unsharded batch: out and dx of each rank's tokens, the
   summed table and bias gradients, over two optimizer steps;
@@ -225,7 +226,11 @@ def _run(worker, world=2, timeout=600):
 
 
 @needs2
-def test_peer_allreduce_matches_nccl():
+@pytest.mark.parametrize("kernel", ["warp", "thread"])
+def test_peer_allreduce_matches_nccl(kernel, monkeypatch):
+    """Both flag-in-word kernels: one warp per (32 pairs, rank), the default
+    for 2, 4 and 8 ranks, and one thread per pair (AIWN_IL_ALLREDUCE=thread)."""
+    monkeypatch.setenv("AIWN_IL_ALLREDUCE", kernel)
     _run(_peer_allreduce_worker)
 
 
@@ -239,13 +244,15 @@ def test_column_sharded_two_ranks_match_oracle():
     _run(_column_shard_worker)
 
 
-@pytest.mark.parametrize("n", [4096, (1 << 21) + 4], ids=["one_word_flags", "two_shot"])
-def test_allreduce_wait_runs_out_and_reports(n):
+@pytest.mark.parametrize("n,kernel", [(4096, "warp"), (4096, "thread"), ((1 << 21) + 4, "warp")],
+                         ids=["flags_in_words_warp", "flags_in_words_thread", "two_shot"])
+def test_allreduce_wait_runs_out_and_reports(n, kernel, monkeypatch):
     """One GPU, a 2-rank all-reduce whose second 'rank' is a local buffer that
     no kernel ever serves: every bounded wait gives up after 50 ms, the
     status reads IL_ERR_TIMEOUT, and the device keeps working.  Both kernels
     (small buffers: flags in the data words; large: per-block barriers)."""
     from aiwn_b200 import _lib
+    monkeypatch.setenv("AIWN_IL_ALLREDUCE", kernel)
     dev = torch.device("cuda", 0)
     sb = _lib.allreduce_scratch_bytes(n, 2)
     bufs = [torch.ones(n + 64, device=dev) for _ in range(2)]
