@@ -106,6 +106,12 @@ __device__ __forceinline__ void srt_walk(const SrtArgs& p, uint32_t slice_s, uin
     }
     int cur = -1;
     float4 tlo = make_float4(0.f, 0.f, 0.f, 0.f), thi = tlo, acl = tlo, ach = tlo;
+    // whole-warp groups (C == 32): the dx partials of an iteration's entries
+    // are reduced together after it (wpart, wtok, wok)
+    constexpr bool kWarpDx = GX && C == 32;
+    float wpart[kSrtDepth];
+    uint32_t wtok[kSrtDepth];
+    bool wok[kSrtDepth];
     for (int b = 0; b < steps; b += kSrtDepth) {
 #pragma unroll
         for (int d = 0; d < kSrtDepth; ++d) {
@@ -148,14 +154,42 @@ __device__ __forceinline__ void srt_walk(const SrtArgs& p, uint32_t slice_s, uin
                 const float dl = g.x * tlo.x + g.y * tlo.y + g.z * tlo.z + g.w * tlo.w;
                 const float dh = g.x * thi.x + g.y * thi.y + g.z * thi.z + g.w * thi.w;
                 float part = w.z * dl + (1.0f - w.z) * dh;
-                // sum over the group's C lanes into its lane 0
+                if constexpr (kWarpDx) {
+                    wpart[d] = part;
+                    wtok[d] = ent & kSrtTokMask;
+                    wok[d] = valid;
+                } else {
+                    // sum over the group's C lanes into its lane 0
 #pragma unroll
-                for (int off = 1; off < C; off <<= 1) {
-                    const float o = __shfl_down_sync(0xffffffffu, part, off);
-                    if (gl + off < C) part += o;
+                    for (int off = 1; off < C; off <<= 1) {
+                        const float o = __shfl_down_sync(0xffffffffu, part, off);
+                        if (gl + off < C) part += o;
+                    }
+                    if (valid && gl == 0)
+                        sts_u32(xd_s + 4u * (uint32_t)(c * TT + (ent & kSrtTokMask)), __float_as_uint(part));
                 }
-                if (valid && gl == 0) sts_u32(xd_s + 4u * (uint32_t)(c * TT + (ent & kSrtTokMask)), __float_as_uint(part));
             }
+        }
+        if constexpr (kWarpDx) {
+            // the up to four partials of this iteration summed over the warp at
+            // once: halves swap at distance 16 and 8 (two values, then one per
+            // lane), then a butterfly over 4, 2, 1; lane 8k ends with entry k's sum
+            static_assert(kSrtDepth <= 4, "four values per reduction");
+            const float a0 = wpart[0], a1 = kSrtDepth > 1 ? wpart[1 % kSrtDepth] : 0.0f;
+            const float a2 = kSrtDepth > 2 ? wpart[2 % kSrtDepth] : 0.0f, a3 = kSrtDepth > 3 ? wpart[3 % kSrtDepth] : 0.0f;
+            const bool h16 = (gl & 16) != 0, h8 = (gl & 8) != 0;
+            float k0 = h16 ? a2 : a0, k1 = h16 ? a3 : a1;
+            k0 += __shfl_xor_sync(0xffffffffu, h16 ? a0 : a2, 16);
+            k1 += __shfl_xor_sync(0xffffffffu, h16 ? a1 : a3, 16);
+            float r = h8 ? k1 : k0;
+            r += __shfl_xor_sync(0xffffffffu, h8 ? k0 : k1, 8);
+            r += __shfl_xor_sync(0xffffffffu, r, 4);
+            r += __shfl_xor_sync(0xffffffffu, r, 2);
+            r += __shfl_xor_sync(0xffffffffu, r, 1);
+            const int k = gl >> 3;
+#pragma unroll
+            for (int d = 0; d < kSrtDepth; ++d)
+                if (k == d && (gl & 7) == 0 && wok[d]) sts_u32(xd_s + 4u * (uint32_t)(c * TT + wtok[d]), __float_as_uint(r));
         }
     }
     if (cur >= 0) {
