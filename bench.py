@@ -230,6 +230,7 @@ def run_reference(args, cfg, world, rank):
     cores = torch.get_num_threads()
     sample = (f"{n_s} of the {N} tokens of the workload per step (fwd+bwd of the reference's "
               f"eager ops, restated in oracle/eager_port.py), {cores} threads")
+    module = None if cfg.get("v2") else reference_module_cpu(cfg, x, go, min(args.steps, 3))
     return {
         "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
@@ -237,9 +238,41 @@ def run_reference(args, cfg, world, rank):
         "impl": "reference",
         "config": arm_config(cfg), "x_dtype": cfg["dtype"],
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "cpu_model": cpu_model(), "kind": "port",
-                         "sample": sample},
+                         "sample": sample, "reference_module": module},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+
+
+def reference_module_cpu(cfg, x, go, steps):
+    """The same CPU step through the reference's own module, installed
+    unchanged in baseline/_ref (its IndexedLinear.forward takes _eager on CPU
+    tensors, aiwn/layers/indexed_linear.py:173-190, and autograd does the
+    backward): a check that the timed port runs at the reference's speed."""
+    if steps < 1 or not os.path.isdir(os.path.join(REF_PKG, "aiwn")):
+        return None
+    try:
+        sys.path.insert(0, REF_PKG)
+        try:
+            import aiwn.layers.indexed_linear as ref_il
+        finally:
+            sys.path.remove(REF_PKG)
+        m = ref_il.IndexedLinear(cfg["IN"], cfg["OUT"], cfg["K"])
+        xr = x.float().clone().requires_grad_(True)
+
+        def step():
+            m.zero_grad(set_to_none=True)
+            xr.grad = None
+            m(xr).backward(go)
+
+        step()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            step()
+        dt = (time.perf_counter() - t0) / steps
+        return {"value": x.shape[0] / dt, "unit": "tokens/s", "steps": steps,
+                "code": "baseline/_ref aiwn.layers.indexed_linear.IndexedLinear on CPU tensors, fwd+bwd"}
+    except Exception as e:  # reported, never fatal
+        return {"unavailable": repr(e)[:200]}
 
 
 REF_CUDA_SO = os.path.join(ROOT, "baseline", "_ref", "indexed_linear_cuda.so")
