@@ -89,24 +89,42 @@ class HostPipeline:
     0.72 ms), while the kernels gain from fine chunks.  A piece of several
     chunks is uploaded with one copy per input, its chunks' forwards run,
     its out leaves with one copy while their backwards run, then its dx.
+    ``pieces`` is a count of equal pieces or a tuple of chunk counts per
+    piece; pieces that shrink towards the end shorten the step's tail (the
+    last piece's kernels and download come after the last upload).
     """
 
     # chunk counts and upload pieces tried when none is given
     TUNE_CHUNKS = (1, 2, 4, 8, 16)
     TUNE_PIECES = (1, 2, 4)
+    TUNE_TAPERED = {8: ((4, 2, 1, 1),), 16: ((5, 5, 3, 2, 1), (6, 4, 3, 2, 1))}
     TUNE_MIN_CHUNK = 4096  # tokens
+    TUNE_STEPS = 5
+    TUNE_FINALISTS = 3
 
     def __init__(self, layer, chunks: int | None = None, device=None, graphs: bool = True,
-                 max_resident_bytes: int = 1 << 30, pieces: int | None = None):
+                 max_resident_bytes: int = 1 << 30, pieces=None):
         self.layer = layer
         inner = getattr(layer, "layer", layer)
         self.inner = inner
         self.auto = chunks is None
         self.chunks = 1 if chunks is None else max(1, int(chunks))
-        # upload pieces: one per chunk unless given (must divide the chunk count)
-        self.pieces = self.chunks if pieces is None else max(1, min(int(pieces), self.chunks))
-        if self.chunks % self.pieces:
-            raise ValueError(f"pieces ({self.pieces}) must divide chunks ({self.chunks})")
+        # copy pieces: one per chunk unless given; an int must divide the chunk
+        # count, a tuple of chunk counts must add up to it
+        if pieces is None:
+            pieces = self.chunks
+        if isinstance(pieces, (tuple, list)):
+            sizes = tuple(int(v) for v in pieces)
+            if not sizes or min(sizes) < 1 or sum(sizes) != self.chunks:
+                raise ValueError(f"piece sizes {sizes} must be >= 1 and add up to chunks ({self.chunks})")
+            self.pieces = sizes
+        else:
+            q = max(1, min(int(pieces), self.chunks))
+            if self.chunks % q:
+                raise ValueError(f"pieces ({q}) must divide chunks ({self.chunks})")
+            self.pieces = q
+            sizes = (self.chunks // q,) * q
+        self.piece_sizes = sizes
         self._tuned = {}  # (N, in, out, x dtype) -> tuned HostPipeline
         self.device = torch.device(device) if device is not None else inner.table.device
         self.s_h2d = torch.cuda.Stream(self.device)
@@ -151,8 +169,8 @@ class HostPipeline:
         n = (N + self.chunks - 1) // self.chunks
         slots, gr, full = self._buffers(n, IN, OUT, x_host.dtype)
         S = len(slots)
-        # upload pieces of cpp chunks each (resident buffers only)
-        cpp = self.chunks // self.pieces if full is not None else 1
+        # copy pieces (resident buffers only; a ring copies per chunk)
+        sizes = self.piece_sizes if full is not None else (1,) * self.chunks
         ws_n = _lib.workspace_bytes(n, IN, OUT, K, _lib.x_dtype_code(slots[0]["x"]))
         if ws_n and (self._ws is None or self._ws.numel() < ws_n):
             self._ws = torch.empty(ws_n, dtype=torch.uint8, device=self.device)
@@ -165,13 +183,18 @@ class HostPipeline:
             s.wait_stream(cur)
         ev = lambda: torch.cuda.Event()  # noqa: E731
         nch = (N + n - 1) // n  # non-empty chunks
-        npieces = (nch + cpp - 1) // cpp
-        # per piece (= per chunk when cpp == 1): x_up, go_up, fwd_done, bwd_done, out_down, gx_down
+        bounds, c0 = [], 0
+        for sz in sizes:
+            if c0 >= nch:
+                break
+            bounds.append((c0, min(nch, c0 + sz)))
+            c0 += sz
+        npieces = len(bounds)
+        # per piece (= per chunk in a ring): x_up, go_up, fwd_done, bwd_done, out_down, gx_down
         x_up, go_up, fwd_done, bwd_done, out_down, gx_down = ([ev() for _ in range(npieces)] for _ in range(6))
-        for q in range(npieces):
-            c0, c1 = q * cpp, min(nch, (q + 1) * cpp)
+        for q, (c0, c1) in enumerate(bounds):
             pa, pb = c0 * n, min(N, c1 * n)
-            if cpp > 1:  # resident: one copy per piece, straight into the whole-batch buffers
+            if full is not None:  # resident: one copy per piece, straight into the whole-batch buffers
                 xq, goq, outq, gxq = (full[k][pa:pb] for k in ("x", "go", "out", "gx"))
             else:
                 sl = slots[q % S]
@@ -213,30 +236,44 @@ class HostPipeline:
         return gr
 
     def _tune(self, x_host, go_host, out_host, gx_host):
-        """The fastest chunk count for this batch shape on this host: host
-        to device copies are slower for small pieces on some hosts while
-        every chunk adds the kernels' fixed cost, so the best split depends
-        on the machine.  Each candidate runs one untimed and three timed
-        steps (gradients stay in the pipeline's own sums)."""
+        """The fastest chunk and piece counts for this batch shape on this
+        host: every pinned copy has a fixed cost while every chunk adds the
+        kernels' fixed cost, so the best split depends on the machine.  Each
+        candidate runs one untimed and TUNE_STEPS timed steps (the fastest
+        step counts; gradients stay in the pipeline's own sums); the best
+        TUNE_FINALISTS are timed once more and the fastest of all is kept."""
         N = x_host.shape[0]
-        cands = [(c, q) for c in self.TUNE_CHUNKS if c == 1 or N // c >= self.TUNE_MIN_CHUNK
-                 for q in sorted(set(self.TUNE_PIECES) | {c}) if q <= c and c % q == 0]
-        best = None
-        for c, q in cands:
-            p = HostPipeline(self.layer, chunks=c, device=self.device, graphs=self.graphs,
-                             max_resident_bytes=self.max_resident_bytes, pieces=q)
-            cur = torch.cuda.current_stream(self.device)
+        cs = [c for c in self.TUNE_CHUNKS if c == 1 or N // c >= self.TUNE_MIN_CHUNK]
+        cands = [(c, q) for c in cs for q in sorted(set(self.TUNE_PIECES) | {c}) if q <= c and c % q == 0]
+        cands += [(c, t) for c in cs for t in self.TUNE_TAPERED.get(c, ())]
+        cur = torch.cuda.current_stream(self.device)
+
+        def make(c, q):
+            return HostPipeline(self.layer, chunks=c, device=self.device, graphs=self.graphs,
+                                max_resident_bytes=self.max_resident_bytes, pieces=q)
+
+        def timed(p):
             p._run(x_host, go_host, out_host, gx_host, True)
             cur.synchronize()
-            t0 = time.perf_counter()
-            for _ in range(3):
+            best_step = None
+            for _ in range(self.TUNE_STEPS):
+                t0 = time.perf_counter()
                 p._run(x_host, go_host, out_host, gx_host, True)
                 cur.synchronize()  # a step ends with its results in host memory
-            dt = time.perf_counter() - t0
-            if best is None or dt < best[0]:
-                best = (dt, p)
+                dt = time.perf_counter() - t0
+                best_step = dt if best_step is None else min(best_step, dt)
+            return best_step
+
+        times = {}
+        for cand in cands:
+            p = make(*cand)
+            times[cand] = timed(p)
             del p
-        return best[1]
+        for cand in sorted(times, key=times.get)[:self.TUNE_FINALISTS]:
+            p = make(*cand)
+            times[cand] = min(times[cand], timed(p))
+            del p
+        return make(*min(times, key=times.get))
 
     def forward_backward(self, x_host, go_host, out_host, gx_host, accumulate_grads: bool = True):
         """out_host <- layer(x_host); gx_host <- d/dx; table.grad/bias.grad +=.
@@ -272,7 +309,8 @@ class HostPipeline:
 
     @property
     def chosen_pieces(self) -> dict:
-        """Upload pieces in use per batch size N (the tuned ones when auto)."""
+        """Copy pieces in use per batch size N (the tuned ones when auto): a
+        count of equal pieces or a tuple of chunk counts."""
         if not self.auto:
             return {"all": self.pieces}
         return {k[0][0]: p.pieces for k, p in self._tuned.items()}

@@ -310,9 +310,10 @@ def test_backward_accumulate_adds_into_grads():
 
 
 @pytest.mark.parametrize("chunks,pieces,resident", [(5, None, True), (5, None, False), (None, None, True),
-                                                    (6, 2, True), (8, 1, True), (6, 3, False)],
+                                                    (6, 2, True), (8, 1, True), (6, 3, False),
+                                                    (7, (3, 2, 1, 1), True), (6, (1, 4, 1), False)],
                          ids=["per_chunk_buffers", "slot_ring", "tuned_chunks", "pieces_of_3_chunks",
-                              "one_upload", "ring_ignores_pieces"])
+                              "one_upload", "ring_ignores_pieces", "tapered_pieces", "ring_ignores_tapered"])
 @pytest.mark.parametrize("graphs", [True, False])
 def test_host_pipeline_matches_whole_batch_call(graphs, chunks, pieces, resident):
     """HostPipeline (chunked, copies overlapped on three streams, replayed
@@ -344,4 +345,8 @@ def test_host_pipeline_matches_whole_batch_call(graphs, chunks, pieces, resident
     normwise_close(m.bias.grad.cpu().numpy(), 2 * gb.cpu().numpy(), GRAD_RTOL, "pipeline gb")
     if chunks is None:
         assert pipe.chosen_chunks[N] in HostPipeline.TUNE_CHUNKS
-        assert pipe.chosen_chunks[N] % pipe.chosen_pieces[N] == 0
+        q, c_ = pipe.chosen_pieces[N], pipe.chosen_chunks[N]
+        if isinstance(q, tuple):
+            assert sum(q) == c_
+        else:
+            assert c_ % q == 0
