@@ -399,6 +399,7 @@ __global__ void __launch_bounds__(kSrtThreads, kSrtCtasPerSm)
         const int q = (r1 - r0 + parts - 1) / parts;
         const int a0 = min(r1, r0 + (int)blockIdx.y * q), a1 = min(r1, a0 + q);
         constexpr int kWarpsPerChunk = (kSrtThreads / 32) / C;
+        static_assert(kWarpsPerChunk >= 1, "every 4-column chunk of a j-range needs a warp for the bias gradient");
         const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
         if (w < kWarpsPerChunk * C) {
             const int c = w % C, wr = w / C;
