@@ -106,9 +106,9 @@ __device__ __forceinline__ void srt_walk(const SrtArgs& p, uint32_t slice_s, uin
     }
     int cur = -1;
     float4 tlo = make_float4(0.f, 0.f, 0.f, 0.f), thi = tlo, acl = tlo, ach = tlo;
-    // whole-warp groups (C == 32): the dx partials of an iteration's entries
-    // are reduced together after it (wpart, wtok, wok)
-    constexpr bool kWarpDx = GX && C == 32;
+    // power-of-two groups of at least 4 lanes: the dx partials of an
+    // iteration's entries are reduced together after it (wpart, wtok, wok)
+    constexpr bool kWarpDx = GX && C >= 4 && (C & (C - 1)) == 0;
     float wpart[kSrtDepth];
     uint32_t wtok[kSrtDepth];
     bool wok[kSrtDepth];
@@ -171,25 +171,27 @@ __device__ __forceinline__ void srt_walk(const SrtArgs& p, uint32_t slice_s, uin
             }
         }
         if constexpr (kWarpDx) {
-            // the up to four partials of this iteration summed over the warp at
-            // once: halves swap at distance 16 and 8 (two values, then one per
-            // lane), then a butterfly over 4, 2, 1; lane 8k ends with entry k's sum
+            // the up to four partials of this iteration summed over the group's
+            // C lanes at once: the group's halves swap at distance C/2 (two
+            // values each), its quarters at C/4 (one value), then a butterfly
+            // over C/8 .. 1; lane k*C/4 of the group ends with entry k's sum.
+            // log2(C) + 1 shuffles for the iteration against 3 log2(C).
             static_assert(kSrtDepth <= 4, "four values per reduction");
+            constexpr int H = C / 2, Q = C / 4;
             const float a0 = wpart[0], a1 = kSrtDepth > 1 ? wpart[1 % kSrtDepth] : 0.0f;
             const float a2 = kSrtDepth > 2 ? wpart[2 % kSrtDepth] : 0.0f, a3 = kSrtDepth > 3 ? wpart[3 % kSrtDepth] : 0.0f;
-            const bool h16 = (gl & 16) != 0, h8 = (gl & 8) != 0;
-            float k0 = h16 ? a2 : a0, k1 = h16 ? a3 : a1;
-            k0 += __shfl_xor_sync(0xffffffffu, h16 ? a0 : a2, 16);
-            k1 += __shfl_xor_sync(0xffffffffu, h16 ? a1 : a3, 16);
-            float r = h8 ? k1 : k0;
-            r += __shfl_xor_sync(0xffffffffu, h8 ? k0 : k1, 8);
-            r += __shfl_xor_sync(0xffffffffu, r, 4);
-            r += __shfl_xor_sync(0xffffffffu, r, 2);
-            r += __shfl_xor_sync(0xffffffffu, r, 1);
-            const int k = gl >> 3;
+            const bool hh = (gl & H) != 0, hq = (gl & Q) != 0;
+            float k0 = hh ? a2 : a0, k1 = hh ? a3 : a1;
+            k0 += __shfl_xor_sync(0xffffffffu, hh ? a0 : a2, H);
+            k1 += __shfl_xor_sync(0xffffffffu, hh ? a1 : a3, H);
+            float r = hq ? k1 : k0;
+            r += __shfl_xor_sync(0xffffffffu, hq ? k0 : k1, Q);
+#pragma unroll
+            for (int off = Q / 2; off >= 1; off >>= 1) r += __shfl_xor_sync(0xffffffffu, r, off);
+            const int k = gl / Q;
 #pragma unroll
             for (int d = 0; d < kSrtDepth; ++d)
-                if (k == d && (gl & 7) == 0 && wok[d]) sts_u32(xd_s + 4u * (uint32_t)(c * TT + wtok[d]), __float_as_uint(r));
+                if (k == d && (gl % Q) == 0 && wok[d]) sts_u32(xd_s + 4u * (uint32_t)(c * TT + wtok[d]), __float_as_uint(r));
         }
     }
     if (cur >= 0) {
