@@ -135,14 +135,17 @@ int forward_dispatch(const void* x, int x_dtype, const float* table, const float
         }
     }
     const KernelChoice path = kernel_choice("AIWN_IL_FORWARD", "token", "cluster");
-    // Rows of a multiple of 128 outputs over at most 128 bins, with tokens
-    // for at least one CTA of 4 warps per SM: the warp-per-token forward
-    // reads each table row as one conflict-free 512-byte line and beat the
-    // cluster and token kernels from 8 K tokens up (16384 x 64 -> 128, K=64:
-    // 46 against 97 us; 65536 x 16 -> 128, K=128: 48 against 99 us; 32768 x
-    // 128 -> 1024, K=32: 1.25 against 4.14 ms), while at 2-4 K tokens its
-    // few CTAs lost (2048 x 64 -> 128, K=16: 30 against 17 us).
-    if (path == kAny && OUT % il::kWideJ == 0 && c.K <= 128 && (N / 64) * (OUT / il::kWideJ) >= sms &&
+    // Rows of a multiple of 128 (or 64) outputs over at most 128 bins, with
+    // tokens for at least one CTA of 4 warps per SM: the warp-per-token
+    // forward reads each table row as conflict-free 128-byte lines and beat
+    // the cluster and token kernels from 8 K tokens up (16384 x 64 -> 128,
+    // K=64: 46 against 97 us; 65536 x 16 -> 128, K=128: 48 against 99 us;
+    // 32768 x 128 -> 1024, K=32: 1.25 against 4.14 ms; 64-wide rows: 131072 x
+    // 64 -> 64, K=16: 168 against 221 us; 32768 x 64 -> 64, K=64: 51 against
+    // 90 us; 131072 x 20 -> 64, K=128: 60 against 113 us), while with fewer
+    // tokens its few CTAs lost (2048 x 64 -> 128, K=16: 30 against 17 us;
+    // 8192 x 64 -> 64, K=16: 31 against 24 us).
+    if (path == kAny && il::wide_jw(OUT) > 0 && c.K <= 128 && (N / 64) * (OUT / il::wide_jw(OUT)) >= sms &&
         il::fast_forward_args_ok(x, x_dtype, table, bias, out, N, IN, OUT, c.K, c)) {
         const int rc = il::wide_forward(x, x_dtype, table, bias, out, N, IN, OUT, c, sms, s);
         if (rc != il::kNotApplicable) {

@@ -1,22 +1,23 @@
 // il_fwd_wide.cuh -- forward for wide rows over few bins: out_d a multiple of
-// 128 and K <= 128, e.g. IndexedLinear(1024, 1024, K=64) with its 256 MB table.
+// 64 and K <= 128, e.g. IndexedLinear(1024, 1024, K=64) with its 256 MB table.
 //
 // The math is aiwn/layers/indexed_linear.py:173-182 (the same as the other
 // forwards): out[n, j] = bias[j] + sum_i x(1-fr) T[lo, i, j] + x fr T[hi, i, j].
 //
-// Layout.  A CTA owns one j-range of 128 output columns and MW*W tokens; each
-// of its W consumer warps owns MW of those tokens and keeps their 128 x MW
-// accumulators in registers (lane l: columns j0+4l .. j0+4l+3 of every token).
-// A warp works on ONE token at a time, so the 32 lanes of a table-row read
-// cover one contiguous 512-byte row of the slice: every quarter-warp reads an
-// aligned 128-byte line, which is conflict-free whatever the row -- the gather
-// kernels' per-lane random rows cost ~8.7 wavefronts per 128-bit load against
-// 4 here.  The row and the two weights of each (token, column) are computed
-// once per warp into shared memory and read back as a broadcast.
+// Layout.  A CTA owns one j-range of JW = 128 (or 64) output columns and MW*W
+// tokens; each of its W consumer warps owns MW of those tokens and keeps their
+// accumulators in registers (lane l: columns j0+4(l%(JW/4)) .. +3).  A warp
+// works on ONE token at a time (JW = 128) or two (JW = 64, one per half-warp),
+// so the lanes of a table-row read cover contiguous 512- (256-) byte rows of
+// the slice: every quarter-warp reads one aligned 128-byte line, which is
+// conflict-free whatever the row -- the gather kernels' per-lane random rows
+// cost ~8.7 wavefronts per 128-bit load against 4 here.  The row and the two
+// weights of each (token, column) are computed once per warp into shared
+// memory and read back as a broadcast.
 //
 // The table streams through kWideStages shared-memory stages of CB input
-// columns each (one TMA box {128 floats, CB columns, K rows}, laid out
-// [K][CB][128]); a producer warp refills a stage once every consumer warp has
+// columns each (one TMA box {JW floats, CB columns, K rows}, laid out
+// [K][CB][JW]); a producer warp refills a stage once every consumer warp has
 // released it (per-stage full/empty mbarriers, bounded waits).
 #pragma once
 #include "il_fast.cuh"
@@ -24,14 +25,15 @@
 
 namespace il {
 
-constexpr int kWideJ = 128;   // output columns per CTA (32 lanes x 4)
 constexpr int kWideEB = 8;    // input columns per block of (row, weight) entries
 constexpr int kWideStages = 3;
-constexpr int kWideStageMax = 64 * 1024;
-constexpr int kWideMW = 16;   // tokens per consumer warp (their accumulators stay in registers)
-// consumer warps per CTA, at most (with the producer warp: 512 threads for MW = 16,
-// so that 128 registers per thread fit; 288 for MW = 32)
-__host__ __device__ constexpr int wide_max_warps(int mw) { return mw >= 32 ? 8 : 15; }
+// tokens per consumer warp: 16 accumulators of float4 per lane either way
+__host__ __device__ constexpr int wide_mw(int jw) { return jw >= 128 ? 16 : 32; }
+// bytes per stage, at most (the 64-wide kernel's entry blocks are twice as large)
+__host__ __device__ constexpr int wide_stage_max(int jw) { return jw >= 128 ? 64 * 1024 : 32 * 1024; }
+// consumer warps per CTA, at most (with the producer warp: 512 threads, so
+// that 128 registers per thread fit)
+__host__ __device__ constexpr int wide_max_warps(int mw) { return mw >= 64 ? 8 : 15; }
 // one warp's entry block: kWideEB columns of MW + 1 entries (16 bytes each; the
 // padding entry staggers the columns over the bank groups, so that the eight
 // lanes of a quarter-warp, one column each, store without conflicts)
@@ -44,13 +46,17 @@ struct WideArgs {
     int N, IN, OUT, K;
     int nchunks;      // IN / CB
     int warps;        // consumer warps; tokens per CTA = MW * warps
-    int stage_bytes;  // K * CB * 512
+    int stage_bytes;  // K * CB * JW * 4
     BinCfg cfg;
 };
 
-template <int DT, int CB, int MW>
-__global__ void __launch_bounds__(32 * (wide_max_warps(MW) + 1), 1)
+template <int DT, int CB, int JW>
+__global__ void __launch_bounds__(32 * (wide_max_warps(wide_mw(JW)) + 1), 1)
     fwd_wide_kernel(const __grid_constant__ CUtensorMap tmap, const WideArgs p) {
+    constexpr int MW = wide_mw(JW);
+    constexpr int LPT = JW / 4;         // lanes per token
+    constexpr int TPS = 32 / LPT;       // tokens per warp step
+    constexpr int NACC = MW / TPS;      // accumulators per lane
     constexpr int kEntryBytes = wide_entry_bytes(MW);
     extern __shared__ unsigned char smem[];
     static_assert(kWideEB % CB == 0, "entry blocks hold whole chunks");
@@ -62,7 +68,7 @@ __global__ void __launch_bounds__(32 * (wide_max_warps(MW) + 1), 1)
     unsigned char* const entries = stages + kWideStages * p.stage_bytes;
     const uint32_t full = smem_addr(entries + W * kEntryBytes);
     const uint32_t empty = full + 8u * kWideStages;
-    const int j0 = blockIdx.y * kWideJ;
+    const int j0 = blockIdx.y * JW;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kWideStages; ++s) {
@@ -93,11 +99,12 @@ __global__ void __launch_bounds__(32 * (wide_max_warps(MW) + 1), 1)
     const int IN = p.IN, K = p.K;
     const int tok0 = (int)blockIdx.x * (MW * W) + warp * MW;
     unsigned char* const ent = entries + warp * kEntryBytes;
-    constexpr uint32_t kRow = 512u;               // one row of one column in a stage
+    constexpr uint32_t kRow = (uint32_t)JW * 4u;      // one row of one column in a stage
     constexpr uint32_t kRowK = (uint32_t)CB * kRow;  // rows k and k+1 of a column
-    float4 acc[MW];
+    const int ts = lane / LPT, cl = lane % LPT;     // token of the step, chunk of the row
+    float4 acc[NACC];
 #pragma unroll
-    for (int m = 0; m < MW; ++m) acc[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < NACC; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
 
     // entry (column c0 + e, token m) at ent + (e * (MW + 1) + m) * 16:
     // {byte offset of row lo, byte offset of row hi, x(1-fr), x fr}.
@@ -138,23 +145,23 @@ __global__ void __launch_bounds__(32 * (wide_max_warps(MW) + 1), 1)
             if (ch >= p.nchunks) break;
             const int st = ch % kWideStages;
             mbar_wait_bounded(full + 8u * st, (uint32_t)((ch / kWideStages) & 1));
-            const unsigned char* const buf = stages + st * p.stage_bytes + 16 * lane;
+            const unsigned char* const buf = stages + st * p.stage_bytes + 16 * cl;
 #pragma unroll 1
             for (int s = 0; s < CB; ++s) {
                 const float4* const e = reinterpret_cast<const float4*>(ent + (cc * CB + s) * (MW + 1) * 16);
 #pragma unroll
-                for (int m = 0; m < MW; ++m) {
-                    const float4 w = e[m];
+                for (int q = 0; q < NACC; ++q) {
+                    const float4 w = e[q * TPS + ts];
                     const float4 tl = *reinterpret_cast<const float4*>(buf + __float_as_uint(w.x));
                     const float4 th = *reinterpret_cast<const float4*>(buf + __float_as_uint(w.y));
-                    acc[m].x = fmaf(w.z, tl.x, acc[m].x);
-                    acc[m].y = fmaf(w.z, tl.y, acc[m].y);
-                    acc[m].z = fmaf(w.z, tl.z, acc[m].z);
-                    acc[m].w = fmaf(w.z, tl.w, acc[m].w);
-                    acc[m].x = fmaf(w.w, th.x, acc[m].x);
-                    acc[m].y = fmaf(w.w, th.y, acc[m].y);
-                    acc[m].z = fmaf(w.w, th.z, acc[m].z);
-                    acc[m].w = fmaf(w.w, th.w, acc[m].w);
+                    acc[q].x = fmaf(w.z, tl.x, acc[q].x);
+                    acc[q].y = fmaf(w.z, tl.y, acc[q].y);
+                    acc[q].z = fmaf(w.z, tl.z, acc[q].z);
+                    acc[q].w = fmaf(w.z, tl.w, acc[q].w);
+                    acc[q].x = fmaf(w.w, th.x, acc[q].x);
+                    acc[q].y = fmaf(w.w, th.y, acc[q].y);
+                    acc[q].z = fmaf(w.w, th.z, acc[q].z);
+                    acc[q].w = fmaf(w.w, th.w, acc[q].w);
                 }
             }
             __syncwarp();
@@ -163,13 +170,13 @@ __global__ void __launch_bounds__(32 * (wide_max_warps(MW) + 1), 1)
         __syncwarp();  // the entry block is rewritten next
     }
 
-    const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + j0) + lane);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + j0) + cl);
 #pragma unroll
-    for (int m = 0; m < MW; ++m) {
-        const int n = tok0 + m;
+    for (int q = 0; q < NACC; ++q) {
+        const int n = tok0 + q * TPS + ts;
         if (n < p.N)
-            *reinterpret_cast<float4*>(p.out + (int64_t)n * p.OUT + j0 + 4 * lane) =
-                make_float4(acc[m].x + b.x, acc[m].y + b.y, acc[m].z + b.z, acc[m].w + b.w);
+            *reinterpret_cast<float4*>(p.out + (int64_t)n * p.OUT + j0 + 4 * cl) =
+                make_float4(acc[q].x + b.x, acc[q].y + b.y, acc[q].z + b.z, acc[q].w + b.w);
     }
 }
 
@@ -177,52 +184,64 @@ __global__ void __launch_bounds__(32 * (wide_max_warps(MW) + 1), 1)
 // host side
 // ---------------------------------------------------------------------------
 struct WidePlan {
-    int CB = 0, warps = 0, stage_bytes = 0, smem = 0;
+    int JW = 0, CB = 0, warps = 0, stage_bytes = 0, smem = 0;
 };
 
-// CB: the most input columns (1, 2, 4 or 8, dividing in_d) whose stage fits
-// 64 KB; W: consumer warps minimising (waves of CTAs) x W, the larger W on ties
+// the warp-per-token forward's j-range width for out_d, 0 when it has none
+inline int wide_jw(int64_t OUT) { return OUT % 128 == 0 ? 128 : (OUT % 64 == 0 ? 64 : 0); }
+
+// JW: 128 when out_d % 128 == 0, else 64 when out_d % 64 == 0.  CB: the most
+// input columns (1, 2, 4 or 8, dividing in_d) whose stage fits the stage
+// limit; W: consumer warps minimising (waves of CTAs) x W, the larger W on ties
 inline bool plan_wide_forward(int64_t N, int K, int IN, int OUT, int sms, WidePlan& pl) {
-    if (OUT % kWideJ != 0 || K < 1 || K > 128 || IN < 1) return false;
+    const int JW = wide_jw(OUT);
+    if (JW == 0 || K < 1 || K > 128 || IN < 1) return false;
+    const int row = JW * 4, smax = wide_stage_max(JW), MW = wide_mw(JW);
     int CB = 8;
-    while (CB > 1 && (CB * K * 512 > kWideStageMax || IN % CB != 0)) CB >>= 1;
-    if (CB * K * 512 > kWideStageMax) return false;
-    const int64_t jr = OUT / kWideJ;
-    constexpr int kMax = wide_max_warps(kWideMW);
+    while (CB > 1 && (CB * K * row > smax || IN % CB != 0)) CB >>= 1;
+    if (CB * K * row > smax) return false;
+    const int64_t jr = OUT / JW;
+    const int kMax = wide_max_warps(MW);
     int best_w = 0;
     int64_t best = 0;
     for (int w = kMax; w >= 4; --w) {
-        const int64_t ctas = (N + kWideMW * w - 1) / (kWideMW * w) * jr;
+        const int64_t ctas = (N + MW * w - 1) / (MW * w) * jr;
         const int64_t cost = (ctas + sms - 1) / sms * w;
         if (best_w == 0 || cost < best) {
             best = cost;
             best_w = w;
         }
     }
+    pl.JW = JW;
     pl.CB = CB;
     pl.warps = best_w;
-    pl.stage_bytes = CB * K * 512;
-    pl.smem = 1024 + kWideStages * pl.stage_bytes + best_w * wide_entry_bytes(kWideMW) + 16 * kWideStages;
+    pl.stage_bytes = CB * K * row;
+    pl.smem = 1024 + kWideStages * pl.stage_bytes + best_w * wide_entry_bytes(MW) + 16 * kWideStages;
     return pl.smem <= kSmemBudget + 1024;
 }
 
-template <int DT, int CB>
+template <int DT, int CB, int JW>
 inline int launch_wide_fwd(const CUtensorMap& map, const WideArgs& a, const WidePlan& pl, cudaStream_t s) {
-    auto kern = fwd_wide_kernel<DT, CB, kWideMW>;
+    auto kern = fwd_wide_kernel<DT, CB, JW>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem) != cudaSuccess) return 4;
-    const dim3 grid((unsigned)ceil_div(a.N, kWideMW * pl.warps), (unsigned)(a.OUT / kWideJ), 1);
+    const dim3 grid((unsigned)ceil_div(a.N, wide_mw(JW) * pl.warps), (unsigned)(a.OUT / JW), 1);
     kern<<<grid, 32 * (pl.warps + 1), pl.smem, s>>>(map, a);
     return 0;
 }
 
-template <int DT>
+template <int DT, int JW>
 inline int launch_wide_fwd_cb(const CUtensorMap& map, const WideArgs& a, const WidePlan& pl, cudaStream_t s) {
     switch (pl.CB) {
-        case 8: return launch_wide_fwd<DT, 8>(map, a, pl, s);
-        case 4: return launch_wide_fwd<DT, 4>(map, a, pl, s);
-        case 2: return launch_wide_fwd<DT, 2>(map, a, pl, s);
-        default: return launch_wide_fwd<DT, 1>(map, a, pl, s);
+        case 8: return launch_wide_fwd<DT, 8, JW>(map, a, pl, s);
+        case 4: return launch_wide_fwd<DT, 4, JW>(map, a, pl, s);
+        case 2: return launch_wide_fwd<DT, 2, JW>(map, a, pl, s);
+        default: return launch_wide_fwd<DT, 1, JW>(map, a, pl, s);
     }
+}
+
+template <int DT>
+inline int launch_wide_fwd_jw(const CUtensorMap& map, const WideArgs& a, const WidePlan& pl, cudaStream_t s) {
+    return pl.JW == 128 ? launch_wide_fwd_cb<DT, 128>(map, a, pl, s) : launch_wide_fwd_cb<DT, 64>(map, a, pl, s);
 }
 
 // kNotApplicable when the shape has no plan
@@ -231,7 +250,7 @@ inline int wide_forward(const void* x, int x_dtype, const float* table, const fl
     WidePlan pl;
     if (!plan_wide_forward(N, c.K, (int)IN, (int)OUT, sms, pl)) return kNotApplicable;
     CUtensorMap map;
-    if (!make_table_map(&map, table, c.K, (int)IN, (int)OUT, kWideJ, c.K, pl.CB)) return kNotApplicable;
+    if (!make_table_map(&map, table, c.K, (int)IN, (int)OUT, pl.JW, c.K, pl.CB)) return kNotApplicable;
     WideArgs a;
     a.x = x;
     a.bias = bias;
@@ -244,7 +263,7 @@ inline int wide_forward(const void* x, int x_dtype, const float* table, const fl
     a.warps = pl.warps;
     a.stage_bytes = pl.stage_bytes;
     a.cfg = c;
-    return x_dtype == kBF16 ? launch_wide_fwd_cb<kBF16>(map, a, pl, s) : launch_wide_fwd_cb<kF32>(map, a, pl, s);
+    return x_dtype == kBF16 ? launch_wide_fwd_jw<kBF16>(map, a, pl, s) : launch_wide_fwd_jw<kF32>(map, a, pl, s);
 }
 
 }  // namespace il

@@ -126,21 +126,25 @@ def test_c4_parity_at_the_bench_launch_size(fwd, monkeypatch):
 
 def _wide_cases():
     from il_cases import Case
-    listed = [c for c in CASES + EDGE_CASES if c.OUT % 128 == 0 and c.K <= 128 and (c.K & (c.K - 1)) == 0]
+    listed = [c for c in CASES + EDGE_CASES if c.OUT % 64 == 0 and c.K <= 128 and (c.K & (c.K - 1)) == 0]
     return listed + [
         Case("wide_in1020_out128_k64", 333, 1020, 128, 64, "wide", "f32", 0.3, 41),  # entry-block tail
         Case("wide_in9_out384_k128", 1000, 9, 384, 128, "wide", "f32", 0.3, 42),     # one column per stage
         Case("wide_in24_out128_k16_bf16", 2049, 24, 128, 16, "wide", "bf16", 0.3, 43),
         Case("wide_in1_out128_k2", 5, 1, 128, 2, "wide", "f32", 0.3, 44),
         Case("wide_in64_out256_k32_n7000", 7000, 64, 256, 32, "clamp_normal", "f32", 0.3, 45),
+        # 64-wide j-ranges: two tokens per warp step
+        Case("wide64_in64_out64_k16_n7000", 7000, 64, 64, 16, "uniform", "f32", 0.3, 46),
+        Case("wide64_in20_out192_k64", 999, 20, 192, 64, "wide", "f32", 0.3, 47),
+        Case("wide64_in7_out64_k128_bf16", 333, 7, 64, 128, "wide", "bf16", 0.3, 48),
     ]
 
 
 @pytest.mark.parametrize("c", _wide_cases(), ids=lambda c: c.name)
 def test_wide_forward_vs_oracle(c, monkeypatch):
-    """The warp-per-token forward (out_d a multiple of 128, K <= 128), pinned
-    with AIWN_IL_FORWARD=wide: partial token tiles, entry blocks past in_d,
-    1..8 input columns per stage, bf16 x."""
+    """The warp-per-token forward (out_d a multiple of 64, K <= 128), pinned
+    with AIWN_IL_FORWARD=wide: 128- and 64-wide j-ranges, partial token
+    tiles, entry blocks past in_d, 1..8 input columns per stage, bf16 x."""
     monkeypatch.setenv("AIWN_IL_FORWARD", "wide")
     x, table, bias, _ = make_inputs(c)
     out = torch.empty(c.N, c.OUT, device=DEV)
@@ -149,11 +153,13 @@ def test_wide_forward_vs_oracle(c, monkeypatch):
     normwise_close(out.cpu().numpy(), ref, FWD_RTOL[c.dtype], f"{c.name} out (wide)")
 
 
-def test_wide_forward_matches_streamed_forward_bitwise(monkeypatch):
-    """Same products in the same order: the warp-per-token forward and the
-    streamed per-lane forward give identical bits, non-finite inputs included."""
+@pytest.mark.parametrize("OUT", [256, 64])
+def test_wide_forward_matches_streamed_forward_bitwise(OUT, monkeypatch):
+    """Same products in the same order: the warp-per-token forward (128- and
+    64-wide j-ranges) and the per-lane token forward give identical bits,
+    non-finite inputs included."""
     g = torch.Generator().manual_seed(9)
-    N, IN, OUT, K = 1500, 40, 256, 64
+    N, IN, K = 1500, 40, 64
     x = torch.rand(N, IN, generator=g) * 2.4 - 1.2
     x[3, 1] = float("inf")
     x[4, 0] = float("-inf")
